@@ -1,0 +1,591 @@
+// C ABI of tarfa_b200: argument checks, workspace layout and launch sequence.
+// Declarations and the reference interface each entry point replaces are in
+// include/tarfa_b200.h.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/tarfa_b200.h"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "int4.cuh"
+#include "router.cuh"
+
+using namespace tarfa;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+// stage-boundary events for profiling (tarfa_b200_set_stage_events)
+constexpr int kMaxStageEvents = 8;
+thread_local cudaEvent_t g_stage_ev[kMaxStageEvents];
+thread_local int g_stage_n = 0;
+
+void stage_mark(int i, cudaStream_t st) {
+  if (i < g_stage_n && g_stage_ev[i]) cudaEventRecord(g_stage_ev[i], st);
+}
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define TARFA_CUDA(call)                                                              \
+  do {                                                                                \
+    cudaError_t e_ = (call);                                                          \
+    if (e_ != cudaSuccess)                                                            \
+      return fail(TARFA_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));    \
+  } while (0)
+
+#define TARFA_CHECK(cond, ...)                                                        \
+  do {                                                                                \
+    if (!(cond)) return fail(TARFA_ERR_INVALID, __VA_ARGS__);                         \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// device status word (one per device; kernels atomicOr error bits into it)
+// ---------------------------------------------------------------------------
+__device__ unsigned g_device_status;
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mu;
+unsigned* g_status_ptr[kMaxDevices];
+int g_sm_count[kMaxDevices];
+
+int device_info(unsigned** status, int* sms) {
+  int dev = 0;
+  TARFA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TARFA_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    TARFA_CUDA(cudaGetSymbolAddress(&p, g_device_status));
+    int n = 0;
+    TARFA_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    g_sm_count[dev] = n;
+    g_status_ptr[dev] = static_cast<unsigned*>(p);
+  }
+  *status = g_status_ptr[dev];
+  *sms = g_sm_count[dev];
+  return TARFA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// workspace layout
+// ---------------------------------------------------------------------------
+struct Ws {
+  size_t counter, logits, gate_logit, idx32, topw, units, perm_tok, perm_slot, route_row, act, y;
+  size_t total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+Ws layout(const tarfa_moe_shape& s, int op) {
+  const int64_t T = s.tokens, K = s.top_k, E = s.experts, H = s.hidden;
+  const int64_t Is = op == TARFA_OP_MOE_LAYER ? s.shared_inter : 0;
+  const int64_t R = T * K;
+  const int64_t Rt = R + (Is > 0 ? T : 0);
+  const int64_t Umax = (R < E ? R : E) + 1;
+  const int64_t Imax = s.inter > Is ? s.inter : Is;
+  Ws w{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t at = o; o += align256(bytes); return at; };
+  w.counter = take(16);
+  w.units = take((4 + 4 * Umax) * 4);
+  w.idx32 = take(R * 4);
+  w.topw = take(R * 4);
+  w.route_row = take(R * 4);
+  w.perm_tok = take((Rt > 0 ? Rt : 1) * 4);
+  w.perm_slot = take(R * 4);
+  if (op == TARFA_OP_MOE_LAYER || op == TARFA_OP_ROUTER) {
+    w.logits = take(T * E * 4);
+    w.gate_logit = take(T * 4);
+  }
+  if (op == TARFA_OP_MOE_LAYER || op == TARFA_OP_EXPERTS) {
+    w.act = take(Rt * Imax * 2);
+    w.y = take(Rt * H * 4);
+  }
+  w.total = o;
+  return w;
+}
+
+template <typename P> P* at(void* base, size_t off) {
+  return reinterpret_cast<P*>(static_cast<char*>(base) + off);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// ---------------------------------------------------------------------------
+// shape / weight validation
+// ---------------------------------------------------------------------------
+int check_shape(const tarfa_moe_shape* s) {
+  TARFA_CHECK(s, "null shape");
+  TARFA_CHECK(s->tokens >= 0 && s->hidden > 0 && s->experts > 0 && s->inter > 0,
+              "bad shape T=%lld H=%lld E=%lld I=%lld", (long long)s->tokens,
+              (long long)s->hidden, (long long)s->experts, (long long)s->inter);
+  TARFA_CHECK(s->dtype == TARFA_BF16 || s->dtype == TARFA_F16, "dtype %d", s->dtype);
+  TARFA_CHECK(s->top_k >= 1 && s->top_k <= 32, "top_k %d not in [1, 32]", s->top_k);
+  if (s->experts > 1024) return fail(TARFA_ERR_UNSUPPORTED, "experts %lld > 1024", (long long)s->experts);
+  TARFA_CHECK(s->hidden % 32 == 0, "hidden %lld not a multiple of 32", (long long)s->hidden);
+  TARFA_CHECK(s->inter % 32 == 0, "inter %lld not a multiple of 32", (long long)s->inter);
+  TARFA_CHECK(s->shared_inter >= 0 && s->shared_inter % 32 == 0, "shared_inter %lld",
+              (long long)s->shared_inter);
+  if (s->hidden > 8192) return fail(TARFA_ERR_UNSUPPORTED, "hidden %lld > 8192", (long long)s->hidden);
+  if (s->tokens * s->top_k > (1ll << 30)) return fail(TARFA_ERR_UNSUPPORTED, "too many routes");
+  return TARFA_OK;
+}
+
+int check_weights(const tarfa_moe_shape* s, const tarfa_moe_weights* w) {
+  TARFA_CHECK(w, "null weights");
+  TARFA_CHECK(w->gate_up && w->down, "null expert weights");
+  TARFA_CHECK(aligned16(w->gate_up) && aligned16(w->down), "expert weights not 16-byte aligned");
+  if (w->kind == TARFA_W_INT4) {
+    TARFA_CHECK(w->gate_up_scale && w->down_scale, "int4 weights need scales");
+    TARFA_CHECK(s->hidden % 128 == 0 && s->inter % 128 == 0,
+                "int4 needs hidden and inter multiples of 128");
+    TARFA_CHECK(w->group == 0 || (w->group % 128 == 0 && s->hidden % w->group == 0 &&
+                                  s->inter % w->group == 0),
+                "int4 group %d must be 0 or a multiple of 128 dividing hidden and inter", w->group);
+  } else {
+    TARFA_CHECK(w->kind == TARFA_W_DENSE, "weight kind %d", w->kind);
+  }
+  return TARFA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// launches
+// ---------------------------------------------------------------------------
+template <typename T, int MODE, int PHASE, int KSPLIT, int NTB>
+int launch_gemv(const GemvArgs& a, int max_tiles, int sms, cudaStream_t st) {
+  constexpr int groups = kGemvWarps / KSPLIT;
+  int grid = (max_tiles + groups - 1) / groups;
+  const int cap = 2 * sms;
+  if (grid > cap) grid = cap;
+  if (grid < 1) grid = 1;
+  gemv_kernel<T, MODE, PHASE, KSPLIT, NTB><<<grid, kGemvThreads, 0, st>>>(a);
+  TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
+}
+
+template <typename T, int MODE, int PHASE, int KSPLIT>
+int launch_gemv_ntb(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStream_t st) {
+  if (T_ <= 8) return launch_gemv<T, MODE, PHASE, KSPLIT, 1>(a, max_tiles, sms, st);
+  return launch_gemv<T, MODE, PHASE, KSPLIT, 2>(a, max_tiles, sms, st);
+}
+
+constexpr int kKsplitGateUp = 8;
+constexpr int kKsplitDown = 4;
+
+template <typename T>
+int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_weights& w,
+                const tarfa_shared_expert* sh, const Ws& L, void* ws, void* out,
+                unsigned* status, int sms, cudaStream_t st) {
+  const int T_ = (int)s.tokens, K = s.top_k, E = (int)s.experts, H = (int)s.hidden;
+  const int I = (int)s.inter, Is = sh ? (int)s.shared_inter : 0;
+  const int Imax = I > Is ? I : Is;
+  const int R = T_ * K;
+  const int Umax = (R < E ? R : E);
+  const bool int4 = w.kind == TARFA_W_INT4;
+  const int mode = !int4 ? kModeExact : (T_ == 1 ? kModeInt4Fused : kModeInt4Dequant);
+  int32_t* units = at<int32_t>(ws, L.units);
+
+  GemvArgs g{};
+  g.units = units;
+  g.E = E;
+  g.expert_slot = w.expert_slot;
+  g.status = status;
+  // ---- gate_up + SiLU*mul -> act -------------------------------------------
+  g.x = hidden;
+  g.ld_x = H;
+  g.perm_tok = at<int32_t>(ws, L.perm_tok);
+  g.N_r = I;
+  g.K_r = H;
+  g.N_s = Is;
+  g.K_s = H;
+  g.sw0 = sh ? sh->gate_proj : nullptr;
+  g.sw1 = sh ? sh->up_proj : nullptr;
+  g.out = at<void>(ws, L.act);
+  g.ld_out = Imax;
+  g.w = w.gate_up;
+  if (int4) {
+    g.w_estride = (int64_t)2 * I * H / 8;
+    g.w_rstride = H / 8;
+    g.sc = w.gate_up_scale;
+    g.s_rstride = w.group ? H / w.group : 1;
+    g.s_estride = (int64_t)2 * I * g.s_rstride;
+    g.group = w.group;
+  } else {
+    g.w_estride = (int64_t)2 * I * H;
+    g.w_rstride = H;
+  }
+  const int tiles_gu = Umax * (I / 8) + (Is ? Is / 8 : 0);
+  int rc;
+  if (!int4) {
+    g.which = 3;
+    rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st);
+  } else {
+    g.which = 1;
+    rc = mode == kModeInt4Fused
+             ? launch_gemv_ntb<T, kModeInt4Fused, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st)
+             : launch_gemv_ntb<T, kModeInt4Dequant, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st);
+    if (rc == TARFA_OK && Is) {
+      GemvArgs gs = g;
+      gs.which = 2;
+      rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(gs, Is / 8, T_, sms, st);
+    }
+  }
+  if (rc) return rc;
+  stage_mark(2, st);
+  // ---- down -> y -------------------------------------------------------------
+  g.x = at<void>(ws, L.act);
+  g.ld_x = Imax;
+  g.perm_tok = nullptr;
+  g.N_r = H;
+  g.K_r = I;
+  g.N_s = H;
+  g.K_s = Is;
+  g.sw0 = sh ? sh->down_proj : nullptr;
+  g.sw1 = nullptr;
+  g.out = at<void>(ws, L.y);
+  g.ld_out = H;
+  g.w = w.down;
+  if (int4) {
+    g.w_estride = (int64_t)H * I / 8;
+    g.w_rstride = I / 8;
+    g.sc = w.down_scale;
+    g.s_rstride = w.group ? I / w.group : 1;
+    g.s_estride = (int64_t)H * g.s_rstride;
+  } else {
+    g.w_estride = (int64_t)H * I;
+    g.w_rstride = I;
+  }
+  const int tiles_dn = (Umax + (Is ? 1 : 0)) * (H / 16);
+  if (!int4) {
+    g.which = 3;
+    rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st);
+  } else {
+    g.which = 1;
+    rc = mode == kModeInt4Fused
+             ? launch_gemv_ntb<T, kModeInt4Fused, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st)
+             : launch_gemv_ntb<T, kModeInt4Dequant, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st);
+    if (rc == TARFA_OK && Is) {
+      GemvArgs gs = g;
+      gs.which = 2;
+      rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(gs, H / 16, T_, sms, st);
+    }
+  }
+  if (rc) return rc;
+  stage_mark(3, st);
+  return TARFA_OK;
+}
+
+template <typename T>
+int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* top_w, bool int4,
+                bool with_shared, void* out, cudaStream_t st) {
+  const int T_ = (int)s.tokens, K = s.top_k, H = (int)s.hidden;
+  CombineArgs c{};
+  c.y = at<float>(ws, L.y);
+  c.route_row = at<int32_t>(ws, L.route_row);
+  c.idx32 = at<int32_t>(ws, L.idx32);
+  c.w = top_w;
+  c.units = at<int32_t>(ws, L.units);
+  c.T = T_;
+  c.K = K;
+  c.H = H;
+  c.E = (int)s.experts;
+  c.order_router = T_ == 1;
+  c.mode = !int4 ? kModeExact : (T_ == 1 ? kModeInt4Fused : kModeInt4Dequant);
+  c.gate_logit = with_shared ? at<float>(ws, L.gate_logit) : nullptr;
+  c.out = out;
+  dim3 grid((H + 255) / 256, T_);
+  combine_kernel<T><<<grid, 256, 0, st>>>(c);
+  TARFA_CUDA(cudaGetLastError());
+  stage_mark(4, st);
+  return TARFA_OK;
+}
+
+int permute_smem_bytes(int nwarps, int E) { return (int)(permute_smem_ints(nwarps, E) * 4); }
+
+template <typename Idx>
+int launch_permute(const Idx* idx, int T_, int K, int E, bool add_shared, const PermuteOut& o,
+                   unsigned* status, cudaStream_t st) {
+  const int threads = 1024;
+  const int smem = permute_smem_bytes(threads / 32, E);
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  TARFA_CUDA(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    TARFA_CUDA(cudaFuncSetAttribute(permute_kernel<Idx>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    permute_smem_bytes(32, 1024)));
+    attr_set[dev] = true;
+  }
+  permute_kernel<Idx><<<1, threads, smem, st>>>(idx, T_, K, E, add_shared ? 1 : 0, o, status);
+  TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
+}
+
+template <typename T>
+int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r, const void* bias,
+                  const void* w_sg, const Ws& L, void* ws, int64_t* idx_out, float* w_out,
+                  float* logits_out, bool permute, bool add_shared, unsigned* status,
+                  cudaStream_t st) {
+  RouterArgs a{};
+  a.h = hidden;
+  a.w_r = w_r;
+  a.bias = bias;
+  a.w_sg = w_sg;
+  a.T = (int)s.tokens;
+  a.H = (int)s.hidden;
+  a.E = (int)s.experts;
+  a.K = s.top_k;
+  a.logits = at<float>(ws, L.logits);
+  a.gate_logit = at<float>(ws, L.gate_logit);
+  a.idx32 = at<int32_t>(ws, L.idx32);
+  a.topw = at<float>(ws, L.topw);
+  a.idx_out = idx_out;
+  a.w_out = w_out;
+  a.logits_out = logits_out;
+  a.counter = at<unsigned>(ws, L.counter);
+  a.do_permute = permute;
+  a.add_shared = add_shared;
+  a.perm = PermuteOut{nullptr, at<int32_t>(ws, L.perm_tok), at<int32_t>(ws, L.perm_slot),
+                      at<int32_t>(ws, L.route_row), at<int32_t>(ws, L.units), nullptr};
+  a.status = status;
+  const int rows = a.E + (w_sg ? 1 : 0);
+  const int warps = kRouterThreads / 32;
+  const int grid = (rows + warps - 1) / warps;
+  const int smem = permute ? permute_smem_bytes(warps, a.E) : 0;
+  const int per_lane = (a.H / 8 + 31) / 32;
+#define TARFA_ROUTER(MC)                                                                  \
+  router_kernel<T, MC><<<grid, kRouterThreads, smem, st>>>(a)
+  if (per_lane <= 2) TARFA_ROUTER(2);
+  else if (per_lane <= 4) TARFA_ROUTER(4);
+  else if (per_lane <= 8) TARFA_ROUTER(8);
+  else if (per_lane <= 16) TARFA_ROUTER(16);
+  else TARFA_ROUTER(32);
+#undef TARFA_ROUTER
+  TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// exported entry points
+// ===========================================================================
+extern "C" {
+
+int tarfa_b200_abi_version(void) { return TARFA_B200_ABI_VERSION; }
+
+const char* tarfa_b200_last_error(void) { return g_last_error.c_str(); }
+
+size_t tarfa_b200_workspace_size(const tarfa_moe_shape* shape, int32_t op) {
+  if (!shape) return 0;
+  return layout(*shape, op).total;
+}
+
+int tarfa_b200_set_stage_events(void* const* events, int32_t n) {
+  if (n < 0 || n > kMaxStageEvents) return fail(TARFA_ERR_INVALID, "stage events %d", n);
+  if (n > 0 && !events) return fail(TARFA_ERR_INVALID, "null events");
+  for (int i = 0; i < kMaxStageEvents; ++i)
+    g_stage_ev[i] = i < n ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  g_stage_n = n;
+  return TARFA_OK;
+}
+
+int tarfa_b200_device_status(uint32_t* status, int32_t clear, void* stream) {
+  unsigned* p = nullptr;
+  int sms = 0;
+  if (int rc = device_info(&p, &sms)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned v = 0;
+  TARFA_CUDA(cudaMemcpyAsync(&v, p, sizeof(v), cudaMemcpyDeviceToHost, st));
+  TARFA_CUDA(cudaStreamSynchronize(st));
+  if (clear) {
+    TARFA_CUDA(cudaMemsetAsync(p, 0, sizeof(unsigned), st));
+    TARFA_CUDA(cudaStreamSynchronize(st));
+  }
+  if (status) *status = v;
+  return TARFA_OK;
+}
+
+int tarfa_b200_permute(const tarfa_moe_shape* shape, const int64_t* top_idx,
+                       int32_t* seg_offsets, int32_t* perm_token, int32_t* perm_slot,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_shape(shape)) return rc;
+  if (shape->tokens == 0) return TARFA_OK;
+  TARFA_CHECK(top_idx && perm_token, "null top_idx / perm_token");
+  const Ws L = layout(*shape, TARFA_OP_PERMUTE);
+  if (workspace_bytes < L.total || !workspace)
+    return fail(TARFA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, L.total);
+  unsigned* status;
+  int sms;
+  if (int rc = device_info(&status, &sms)) return rc;
+  PermuteOut o{seg_offsets, perm_token, perm_slot, nullptr, at<int32_t>(workspace, L.units), nullptr};
+  return launch_permute<int64_t>(top_idx, (int)shape->tokens, shape->top_k, (int)shape->experts,
+                                 false, o, status, static_cast<cudaStream_t>(stream));
+}
+
+int tarfa_b200_router_topk(const tarfa_moe_shape* shape, const void* hidden,
+                           const void* router_weight, const void* router_bias,
+                           int64_t* top_idx, float* top_w, float* logits_out,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_shape(shape)) return rc;
+  if (shape->tokens == 0) return TARFA_OK;
+  TARFA_CHECK(hidden && router_weight && top_idx && top_w, "null router argument");
+  TARFA_CHECK(aligned16(hidden) && aligned16(router_weight), "router operands not 16-byte aligned");
+  TARFA_CHECK(shape->top_k <= shape->experts, "top_k > experts");
+  const Ws L = layout(*shape, TARFA_OP_ROUTER);
+  if (workspace_bytes < L.total || !workspace)
+    return fail(TARFA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, L.total);
+  unsigned* status;
+  int sms;
+  if (int rc = device_info(&status, &sms)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (shape->dtype == TARFA_BF16)
+    return launch_router<__nv_bfloat16>(*shape, hidden, router_weight, router_bias, nullptr, L,
+                                        workspace, top_idx, top_w, logits_out, false, false,
+                                        status, st);
+  return launch_router<__half>(*shape, hidden, router_weight, router_bias, nullptr, L, workspace,
+                               top_idx, top_w, logits_out, false, false, status, st);
+}
+
+int tarfa_b200_experts_forward(const tarfa_moe_shape* shape, const void* hidden,
+                               const int64_t* top_idx, const float* top_w,
+                               const tarfa_moe_weights* weights, void* out,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_shape(shape)) return rc;
+  if (int rc = check_weights(shape, weights)) return rc;
+  if (shape->tokens == 0) return TARFA_OK;
+  TARFA_CHECK(hidden && top_idx && top_w && out, "null argument");
+  TARFA_CHECK(aligned16(hidden), "hidden not 16-byte aligned");
+  const Ws L = layout(*shape, TARFA_OP_EXPERTS);
+  if (workspace_bytes < L.total || !workspace)
+    return fail(TARFA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, L.total);
+  unsigned* status;
+  int sms;
+  if (int rc = device_info(&status, &sms)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int T_ = (int)shape->tokens, K = shape->top_k, E = (int)shape->experts;
+  PermuteOut o{nullptr, at<int32_t>(workspace, L.perm_tok), at<int32_t>(workspace, L.perm_slot),
+               at<int32_t>(workspace, L.route_row), at<int32_t>(workspace, L.units),
+               at<int32_t>(workspace, L.idx32)};
+  stage_mark(0, st);
+  if (int rc = launch_permute<int64_t>(top_idx, T_, K, E, false, o, status, st)) return rc;
+  stage_mark(1, st);
+  const bool int4 = weights->kind == TARFA_W_INT4;
+  int rc;
+  if (shape->dtype == TARFA_BF16) {
+    rc = run_experts<__nv_bfloat16>(*shape, hidden, *weights, nullptr, L, workspace, out, status, sms, st);
+    if (!rc) rc = run_combine<__nv_bfloat16>(*shape, L, workspace, top_w, int4, false, out, st);
+  } else {
+    rc = run_experts<__half>(*shape, hidden, *weights, nullptr, L, workspace, out, status, sms, st);
+    if (!rc) rc = run_combine<__half>(*shape, L, workspace, top_w, int4, false, out, st);
+  }
+  return rc;
+}
+
+int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
+                         const void* router_weight, const void* router_bias,
+                         const tarfa_moe_weights* weights, const tarfa_shared_expert* shared,
+                         void* out, int64_t* top_idx_out, float* top_w_out,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_shape(shape)) return rc;
+  if (int rc = check_weights(shape, weights)) return rc;
+  if (shape->tokens == 0) return TARFA_OK;
+  TARFA_CHECK(hidden && router_weight && out, "null argument");
+  TARFA_CHECK(aligned16(hidden) && aligned16(router_weight), "operands not 16-byte aligned");
+  TARFA_CHECK(shape->top_k <= shape->experts, "top_k > experts");
+  const bool has_shared = shared && shape->shared_inter > 0;
+  if (has_shared) {
+    TARFA_CHECK(shared->gate_proj && shared->up_proj && shared->down_proj && shared->gate_weight,
+                "null shared-expert weight");
+    TARFA_CHECK(aligned16(shared->gate_proj) && aligned16(shared->up_proj) &&
+                    aligned16(shared->down_proj) && aligned16(shared->gate_weight),
+                "shared-expert weights not 16-byte aligned");
+  }
+  tarfa_moe_shape s = *shape;
+  if (!has_shared) s.shared_inter = 0;
+  const Ws L = layout(s, TARFA_OP_MOE_LAYER);
+  if (workspace_bytes < L.total || !workspace)
+    return fail(TARFA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, L.total);
+  unsigned* status;
+  int sms;
+  if (int rc = device_info(&status, &sms)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool int4 = weights->kind == TARFA_W_INT4;
+  const tarfa_shared_expert* sh = has_shared ? shared : nullptr;
+  int rc;
+  stage_mark(0, st);
+  if (s.dtype == TARFA_BF16) {
+    rc = launch_router<__nv_bfloat16>(s, hidden, router_weight, router_bias,
+                                      sh ? sh->gate_weight : nullptr, L, workspace, top_idx_out,
+                                      top_w_out, nullptr, true, sh != nullptr, status, st);
+    if (!rc) stage_mark(1, st);
+    if (!rc) rc = run_experts<__nv_bfloat16>(s, hidden, *weights, sh, L, workspace, out, status, sms, st);
+    if (!rc) rc = run_combine<__nv_bfloat16>(s, L, workspace, at<float>(workspace, L.topw), int4, sh != nullptr, out, st);
+  } else {
+    rc = launch_router<__half>(s, hidden, router_weight, router_bias,
+                               sh ? sh->gate_weight : nullptr, L, workspace, top_idx_out,
+                               top_w_out, nullptr, true, sh != nullptr, status, st);
+    if (!rc) stage_mark(1, st);
+    if (!rc) rc = run_experts<__half>(s, hidden, *weights, sh, L, workspace, out, status, sms, st);
+    if (!rc) rc = run_combine<__half>(s, L, workspace, at<float>(workspace, L.topw), int4, sh != nullptr, out, st);
+  }
+  return rc;
+}
+
+int tarfa_b200_dequant_int4(const int32_t* packed, const void* scale, int64_t rows, int64_t cols,
+                            int32_t group, int32_t dtype, void* out, void* stream) {
+  TARFA_CHECK(packed && scale && out, "null argument");
+  TARFA_CHECK(rows >= 0 && cols > 0 && cols % 8 == 0, "bad shape %lld x %lld", (long long)rows,
+              (long long)cols);
+  TARFA_CHECK(group == 0 || (group % 8 == 0 && cols % group == 0), "bad group %d", group);
+  TARFA_CHECK(aligned16(out), "out not 16-byte aligned");
+  if (rows == 0) return TARFA_OK;
+  const int64_t n = rows * (cols / 8);
+  const int threads = 256;
+  const int64_t grid = (n + threads - 1) / threads;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TARFA_BF16)
+    dequant_int4_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(
+        reinterpret_cast<const uint32_t*>(packed), static_cast<const __nv_bfloat16*>(scale), rows,
+        cols, group, static_cast<__nv_bfloat16*>(out));
+  else if (dtype == TARFA_F16)
+    dequant_int4_kernel<__half><<<grid, threads, 0, st>>>(
+        reinterpret_cast<const uint32_t*>(packed), static_cast<const __half*>(scale), rows, cols,
+        group, static_cast<__half*>(out));
+  else
+    return fail(TARFA_ERR_INVALID, "dtype %d", dtype);
+  TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
+}
+
+int tarfa_b200_quantize_int4(const void* w, int64_t rows, int64_t cols, int32_t group,
+                             int32_t* packed, void* scale, void* stream) {
+  TARFA_CHECK(w && packed && scale, "null argument");
+  TARFA_CHECK(rows >= 0 && cols > 0, "bad shape");
+  TARFA_CHECK(group % 128 == 0 && group >= 128 && group <= 1024 && cols % group == 0,
+              "group %d must be a multiple of 128 in [128, 1024] dividing cols", group);
+  TARFA_CHECK(aligned16(w), "w not 16-byte aligned");
+  if (rows == 0) return TARFA_OK;
+  const int64_t warps = rows * (cols / group);
+  const int threads = 256;
+  const int64_t grid = (warps * 32 + threads - 1) / threads;
+  quantize_int4_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(w), rows, cols, group, reinterpret_cast<uint32_t*>(packed),
+      static_cast<__nv_bfloat16*>(scale));
+  TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
+}
+
+}  // extern "C"

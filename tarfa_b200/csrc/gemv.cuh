@@ -1,0 +1,335 @@
+// Grouped expert GEMV for decode-shaped batches (few tokens per expert).
+//
+// One launch computes, for every "unit" (a routed expert with the rows routed
+// to it, or the shared expert with all tokens), either
+//   phase GATE_UP: act[row, i] = silu(gate_i . x_row) * (up_i . x_row)
+//   phase DOWN:    y[row, h]   = down_h . act_row
+// with fp32 accumulation on the tensor cores (mma.sync m16n8k16).  The weights
+// are the only large operand: each weight element is read from HBM exactly
+// once per launch with 128-bit non-allocating loads, so the kernel is bounded
+// by HBM bandwidth; the token vectors (<= 16 per expert at decode) are tiny
+// and stay in L1/L2.
+//
+// A tile is 16 weight rows of one unit.  GATE_UP pairs gate row i with up row
+// I+i in the same tile (rows 0-7 gate, 8-15 up), so one lane ends up holding
+// gate and up of the same (i, token) and applies SiLU*mul in registers.  The K
+// dimension of a tile is split across KSPLIT warps and reduced through shared
+// memory in a fixed order (deterministic results).
+//
+// K permutation.  The MMA only needs A and B to agree on which k a lane holds.
+// A lane loads 16 contiguous bytes of a weight row and the matching 16 bytes
+// of the token vector; both are fed to the same fragment slots, so the dot
+// product is unchanged while every load stays 128-bit and coalesced
+// (4 lanes read 64 contiguous bytes of a row).  For int4, a 32-bit word holds
+// 8 consecutive k; nibbles s and s+4 form one packed (q-8) pair, and the
+// token vector is byte-permuted the same way.
+#pragma once
+#include "common.cuh"
+
+namespace tarfa {
+
+enum GemvPhase { kGateUp = 0, kDown = 1 };
+// kModeExact: dense weights, the exact path's rounding points
+//   (fused_int4.py:191-194 and 240-244).
+// kModeInt4Fused: int4, the fused decode kernel's arithmetic
+//   (moe_kernel.py:27-104: scale folded after the dot, fp32 intermediates).
+// kModeInt4Dequant: int4 dequantised to the model dtype, then the exact path
+//   (fused_int4.py:254-260 with channel_q4.py:10-14).
+enum GemvMode { kModeExact = 0, kModeInt4Fused = 1, kModeInt4Dequant = 2 };
+
+// Unit table written by the permute stage:
+//   hdr[0] routed units, hdr[1] routed rows, hdr[2] has shared unit, hdr[3] shared row0
+//   desc[u] = {expert, row0, nrows, 0}; routed units in ascending expert id,
+//   the shared unit (expert == E) last.
+struct UnitDesc { int expert, row0, nrows, pad; };
+TARFA_DEVI const UnitDesc* unit_descs(const int32_t* units) {
+  return reinterpret_cast<const UnitDesc*>(units + 4);
+}
+
+struct GemvArgs {
+  const void* x;             // GATE_UP: hidden [T, ld_x]; DOWN: act [R, ld_x]
+  int64_t ld_x;
+  const int32_t* perm_tok;   // GATE_UP: row -> token; DOWN: unused (row = x row)
+  const int32_t* units;
+  int which;                 // bit 0: routed units, bit 1: shared unit (dense kernels only)
+  int E;
+  const void* w;             // routed weights: GATE_UP gate_up base, DOWN down base
+  int64_t w_estride;         // per expert (elements, or 32-bit words for int4)
+  int64_t w_rstride;         // per row
+  const void* sc;            // int4 scales
+  int64_t s_estride, s_rstride;
+  int group;                 // int4: 0 = one scale per row, else the group size
+  const int32_t* expert_slot;
+  int N_r, K_r;              // routed: GATE_UP (I, H); DOWN (H, I)
+  const void* sw0;           // shared: GATE_UP gate_proj; DOWN down_proj
+  const void* sw1;           // shared: GATE_UP up_proj
+  int N_s, K_s;              // shared: GATE_UP (Is, H); DOWN (H, Is)
+  void* out;                 // GATE_UP: act (model dtype); DOWN: y (fp32)
+  int64_t ld_out;
+  unsigned* status;
+};
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+
+TARFA_DEVI void group_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+template <typename T, int MODE, int PHASE, int KSPLIT, int NTB>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a) {
+  constexpr bool INT4 = MODE != kModeExact;
+  constexpr int kGroups = kGemvWarps / KSPLIT;              // tiles per CTA step
+  constexpr int TR = PHASE == kGateUp ? 8 : 16;             // tile rows per unit index
+  __shared__ float red[kGroups][KSPLIT][NTB * 4][32];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = warp / KSPLIT, kw = warp % KSPLIT;
+  const int g = lane >> 2, c = lane & 3;
+
+  const int32_t* hdr = a.units;
+  const int nu = hdr[0];
+  const int has_sh = hdr[2];
+  const UnitDesc* descs = unit_descs(a.units);
+  const int tiles_r = a.N_r / TR, tiles_s = a.N_s / TR;
+  const int nt_r = (a.which & 1) ? nu * tiles_r : 0;
+  const int nt_s = (!INT4 && (a.which & 2) && has_sh) ? tiles_s : 0;
+  const int ntiles = nt_r + nt_s;
+
+  for (int base = blockIdx.x * kGroups; base < ntiles; base += gridDim.x * kGroups) {
+    const int tile = base + grp;
+    if (tile >= ntiles) continue;   // uniform within a warp group; groups sync separately
+    // -------- resolve the tile ------------------------------------------------
+    bool shared_unit = false;
+    int tt = 0, K = 0;
+    UnitDesc d;
+    const char* rowA = nullptr;   // weight row for fragment rows g   (bytes)
+    const char* rowB = nullptr;   // weight row for fragment rows g+8
+    const T* scA = nullptr;       // int4 scale rows
+    const T* scB = nullptr;
+    if (tile < nt_r) {
+      const int u = tile / tiles_r;
+      tt = tile % tiles_r;
+      d = descs[u];
+      const int slot = a.expert_slot ? a.expert_slot[d.expert] : d.expert;
+      K = a.K_r;
+      const int ra = PHASE == kGateUp ? tt * 8 + g : tt * 16 + g;
+      const int rb = PHASE == kGateUp ? a.N_r + tt * 8 + g : tt * 16 + g + 8;
+      const int64_t esz = INT4 ? 4 : (int64_t)sizeof(T);
+      const char* wb = static_cast<const char*>(a.w) + (int64_t)slot * a.w_estride * esz;
+      rowA = wb + (int64_t)ra * a.w_rstride * esz;
+      rowB = wb + (int64_t)rb * a.w_rstride * esz;
+      if (INT4) {
+        const T* sb = static_cast<const T*>(a.sc) + (int64_t)slot * a.s_estride;
+        scA = sb + (int64_t)ra * a.s_rstride;
+        scB = sb + (int64_t)rb * a.s_rstride;
+      }
+    } else {
+      shared_unit = true;
+      tt = tile - nt_r;
+      d = descs[nu];
+      K = a.K_s;
+      const T* s0 = static_cast<const T*>(a.sw0);
+      if (PHASE == kGateUp) {
+        rowA = reinterpret_cast<const char*>(s0 + (int64_t)(tt * 8 + g) * K);
+        rowB = reinterpret_cast<const char*>(static_cast<const T*>(a.sw1) + (int64_t)(tt * 8 + g) * K);
+      } else {
+        rowA = reinterpret_cast<const char*>(s0 + (int64_t)(tt * 16 + g) * K);
+        rowB = reinterpret_cast<const char*>(s0 + (int64_t)(tt * 16 + g + 8) * K);
+      }
+    }
+    (void)shared_unit;
+    const int ntok = d.nrows;
+    const int ntb_groups = (ntok + 8 * NTB - 1) / (8 * NTB);
+
+    for (int tg = 0; tg < ntb_groups; ++tg) {
+      float acc[NTB][4];
+#pragma unroll
+      for (int b = 0; b < NTB; ++b)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[b][q] = 0.f;
+
+      // token vector rows for this lane (B fragment column g of each token block)
+      const char* xrow[NTB];
+#pragma unroll
+      for (int b = 0; b < NTB; ++b) {
+        const int n = tg * 8 * NTB + b * 8 + g;
+        xrow[b] = nullptr;
+        if (n < ntok) {
+          const int r = d.row0 + n;
+          const int xr = PHASE == kGateUp ? a.perm_tok[r] : r;
+          xrow[b] = reinterpret_cast<const char*>(static_cast<const T*>(a.x) + (int64_t)xr * a.ld_x);
+        }
+      }
+
+      if (!INT4) {
+        const int n_it = K / 32;
+        const int i0 = kw * n_it / KSPLIT, i1 = (kw + 1) * n_it / KSPLIT;
+        int it = i0;
+        constexpr int NB = 4;
+        for (; it + NB <= i1; it += NB) {
+          uint4 wa[NB], wb2[NB];
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
+            wa[j] = ld_stream(rowA + off);
+            wb2[j] = ld_stream(rowB + off);
+          }
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
+#pragma unroll
+            for (int b = 0; b < NTB; ++b) {
+              uint4 xv = make_uint4(0, 0, 0, 0);
+              if (xrow[b]) xv = ld_cached(xrow[b] + off);
+              Mma<T>::run(acc[b], wa[j].x, wb2[j].x, wa[j].y, wb2[j].y, xv.x, xv.y);
+              Mma<T>::run(acc[b], wa[j].z, wb2[j].z, wa[j].w, wb2[j].w, xv.z, xv.w);
+            }
+          }
+        }
+        for (; it < i1; ++it) {
+          const int64_t off = ((int64_t)it * 32 + c * 8) * (int64_t)sizeof(T);
+          const uint4 wa = ld_stream(rowA + off), wb2 = ld_stream(rowB + off);
+#pragma unroll
+          for (int b = 0; b < NTB; ++b) {
+            uint4 xv = make_uint4(0, 0, 0, 0);
+            if (xrow[b]) xv = ld_cached(xrow[b] + off);
+            Mma<T>::run(acc[b], wa.x, wb2.x, wa.y, wb2.y, xv.x, xv.y);
+            Mma<T>::run(acc[b], wa.z, wb2.z, wa.w, wb2.w, xv.z, xv.w);
+          }
+        }
+      } else {
+        // one iteration = 128 k; lane c covers k [32c, 32c+32) of it
+        const int n_it = K / 128;
+        const int i0 = kw * n_it / KSPLIT, i1 = (kw + 1) * n_it / KSPLIT;
+        const bool grp_scale = a.group != 0;
+        for (int it = i0; it < i1; ++it) {
+          const int64_t woff = ((int64_t)it * 16 + c * 4) * 4;   // bytes
+          const uint4 qa = ld_stream(rowA + woff), qb = ld_stream(rowB + woff);
+          float sa = 1.f, sb = 1.f;
+          uint32_t sa2 = 0, sb2 = 0;
+          if (grp_scale || MODE == kModeInt4Dequant) {
+            const int gi = grp_scale ? (it * 128) / a.group : 0;
+            const uint16_t ua = reinterpret_cast<const uint16_t*>(scA)[gi];
+            const uint16_t ub = reinterpret_cast<const uint16_t*>(scB)[gi];
+            sa = Elem<T>::bits_to_f(ua);
+            sb = Elem<T>::bits_to_f(ub);
+            sa2 = uint32_t(ua) | (uint32_t(ua) << 16);
+            sb2 = uint32_t(ub) | (uint32_t(ub) << 16);
+          }
+          float part[NTB][4];
+#pragma unroll
+          for (int b = 0; b < NTB; ++b)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) part[b][q] = 0.f;
+          const uint32_t qaw[4] = {qa.x, qa.y, qa.z, qa.w};
+          const uint32_t qbw[4] = {qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            uint32_t pa[4], pb[4];
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+              pa[s] = nib_pair<T>(qaw[m], s);
+              pb[s] = nib_pair<T>(qbw[m], s);
+              if (MODE == kModeInt4Dequant) {
+                pa[s] = Mma<T>::mul2(pa[s], sa2);
+                pb[s] = Mma<T>::mul2(pb[s], sb2);
+              }
+            }
+            const int64_t xoff = ((int64_t)it * 128 + c * 32 + m * 8) * (int64_t)sizeof(T);
+#pragma unroll
+            for (int b = 0; b < NTB; ++b) {
+              uint4 xv = make_uint4(0, 0, 0, 0);
+              if (xrow[b]) xv = ld_cached(xrow[b] + xoff);
+              // (x0,x4) (x1,x5) (x2,x6) (x3,x7) to match nibble pairs (s, s+4)
+              const uint32_t x04 = __byte_perm(xv.x, xv.z, 0x5410);
+              const uint32_t x15 = __byte_perm(xv.x, xv.z, 0x7632);
+              const uint32_t x26 = __byte_perm(xv.y, xv.w, 0x5410);
+              const uint32_t x37 = __byte_perm(xv.y, xv.w, 0x7632);
+              if (MODE == kModeInt4Fused && grp_scale) {
+                Mma<T>::run(part[b], pa[0], pb[0], pa[1], pb[1], x04, x15);
+                Mma<T>::run(part[b], pa[2], pb[2], pa[3], pb[3], x26, x37);
+              } else {
+                Mma<T>::run(acc[b], pa[0], pb[0], pa[1], pb[1], x04, x15);
+                Mma<T>::run(acc[b], pa[2], pb[2], pa[3], pb[3], x26, x37);
+              }
+            }
+          }
+          if (MODE == kModeInt4Fused && grp_scale) {
+#pragma unroll
+            for (int b = 0; b < NTB; ++b) {
+              acc[b][0] = fmaf(part[b][0], sa, acc[b][0]);
+              acc[b][1] = fmaf(part[b][1], sa, acc[b][1]);
+              acc[b][2] = fmaf(part[b][2], sb, acc[b][2]);
+              acc[b][3] = fmaf(part[b][3], sb, acc[b][3]);
+            }
+          }
+        }
+      }
+
+      // -------- cross-warp K reduction (fixed order) ---------------------------
+      if (KSPLIT > 1) {
+#pragma unroll
+        for (int b = 0; b < NTB; ++b)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) red[grp][kw][b * 4 + q][lane] = acc[b][q];
+        group_barrier(1 + grp, KSPLIT * 32);
+        if (kw == 0) {
+#pragma unroll
+          for (int b = 0; b < NTB; ++b)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float s = red[grp][0][b * 4 + q][lane];
+#pragma unroll
+              for (int w2 = 1; w2 < KSPLIT; ++w2) s += red[grp][w2][b * 4 + q][lane];
+              acc[b][q] = s;
+            }
+        }
+        group_barrier(1 + grp, KSPLIT * 32);
+      }
+
+      // -------- epilogue --------------------------------------------------------
+      if (kw == 0) {
+        float rsa = 1.f, rsb = 1.f;   // per-row int4 scale, folded after the dot
+        if (MODE == kModeInt4Fused && a.group == 0) {
+          rsa = Elem<T>::bits_to_f(reinterpret_cast<const uint16_t*>(scA)[0]);
+          rsb = Elem<T>::bits_to_f(reinterpret_cast<const uint16_t*>(scB)[0]);
+        }
+#pragma unroll
+        for (int b = 0; b < NTB; ++b)
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int n = tg * 8 * NTB + b * 8 + 2 * c + q;
+            if (n >= ntok) continue;
+            const int r = d.row0 + n;
+            const float va = acc[b][q] * rsa;       // row g   (gate / down row g)
+            const float vb = acc[b][2 + q] * rsb;   // row g+8 (up   / down row g+8)
+            if (PHASE == kGateUp) {
+              float act;
+              if (MODE == kModeInt4Fused) {
+                // moe_kernel.py:99-100: silu(g) * u in fp32, one rounding
+                act = silu_f(va) * vb;
+              } else {
+                // fused_int4.py:193 / 242: F.linear output, silu and product each rounded
+                const float gr = rnd<T>(va), ur = rnd<T>(vb);
+                act = rnd<T>(silu_f(gr)) * ur;
+              }
+              T* o = static_cast<T*>(a.out) + (int64_t)r * a.ld_out + tt * 8 + g;
+              *o = Elem<T>::from_f(act);
+            } else {
+              float* o = static_cast<float*>(a.out) + (int64_t)r * a.ld_out + tt * 16 + g;
+              if (MODE == kModeInt4Fused) {
+                o[0] = va;            // moe_kernel.py:101-102: fp32 per-expert output
+                o[8] = vb;
+              } else {
+                o[0] = rnd<T>(va);    // F.linear(..., dn) output in the model dtype
+                o[8] = rnd<T>(vb);
+              }
+            }
+          }
+      }
+    }
+  }
+}
+
+}  // namespace tarfa

@@ -1,0 +1,267 @@
+"""Torch-tensor wrappers over the C ABI (device memory and streams come from torch).
+
+Each wrapper checks shapes, dtypes, devices and contiguity, passes raw device
+pointers plus the current CUDA stream to ``libtarfa_b200.so`` and raises
+``RuntimeError`` (``TarfaError``) on a non-zero return.  Nothing here computes
+on the CPU: a CPU tensor is an error, and a missing library is an error.
+
+Scratch: every device gets one zero-filled workspace buffer, grown on demand;
+the kernels return its counters to zero, so consecutive calls on one stream
+can share it.  Callers that launch on several streams at once must pass their
+own ``workspace`` tensors.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+import threading
+
+import torch
+
+from . import _capi as api
+
+_DT = {torch.bfloat16: api.TARFA_BF16, torch.float16: api.TARFA_F16}
+_ws_lock = threading.Lock()
+_ws: dict[int, torch.Tensor] = {}
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
+
+
+def _stream(device) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("tarfa_b200 ops take CUDA tensors only (no CPU path)")
+        if not t.is_contiguous():
+            raise RuntimeError("tarfa_b200 ops take contiguous tensors")
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    """Shared zero-filled scratch of at least ``nbytes`` on ``device``."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        buf = _ws.get(idx)
+        if buf is None or buf.numel() < nbytes:
+            if buf is not None:
+                torch.cuda.current_stream(dev).synchronize()
+            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+            _ws[idx] = buf
+        return buf
+
+
+def _shape(T, H, E, I, Is, K, dtype) -> api.MoeShape:
+    if dtype not in _DT:
+        raise RuntimeError(f"unsupported dtype {dtype}; bf16 or fp16")
+    return api.MoeShape(T, H, E, I, Is, K, _DT[dtype])
+
+
+@dataclasses.dataclass
+class ExpertWeights:
+    """Routed-expert weights of one layer, resident on the device.
+
+    kind ``"dense"``: ``gate_up [E, 2I, H]``, ``down [E, H, I]`` in the model dtype.
+    kind ``"int4"``: ``gate_up`` int32 ``[E, 2I, H/8]`` (or uint8 ``[E, 2I, H/2]``),
+    ``down`` int32 ``[E, H, I/8]``, scales in the model dtype ``[E, N, K/group]``
+    (``group`` > 0) or ``[E, N]`` (``group == 0``, the reference's per-row layout).
+    ``expert_slot`` (optional int32 ``[E]``): expert ``e`` is stored at index
+    ``expert_slot[e]`` of the stacks (used by a streaming tier).
+    """
+    gate_up: torch.Tensor
+    down: torch.Tensor
+    kind: str = "dense"
+    gate_up_scale: torch.Tensor | None = None
+    down_scale: torch.Tensor | None = None
+    group: int = 0
+    expert_slot: torch.Tensor | None = None
+
+    def c_struct(self) -> api.MoeWeights:
+        _need_cuda(self.gate_up, self.down, self.gate_up_scale, self.down_scale, self.expert_slot)
+        kind = api.TARFA_W_INT4 if self.kind == "int4" else api.TARFA_W_DENSE
+        if self.expert_slot is not None and self.expert_slot.dtype != torch.int32:
+            raise RuntimeError("expert_slot must be int32")
+        return api.MoeWeights(kind, int(self.group), _ptr(self.gate_up), _ptr(self.gate_up_scale),
+                              _ptr(self.down), _ptr(self.down_scale), _ptr(self.expert_slot))
+
+    def dims(self, H: int):
+        """(E, I) inferred from the stacks."""
+        E = self.gate_up.shape[0]
+        I = self.gate_up.shape[1] // 2
+        return E, I
+
+
+@dataclasses.dataclass
+class SharedWeights:
+    """Shared expert (``Qwen3_5MoeMLP``) and its sigmoid gate, model dtype."""
+    gate_proj: torch.Tensor   # [Is, H]
+    up_proj: torch.Tensor     # [Is, H]
+    down_proj: torch.Tensor   # [H, Is]
+    gate_weight: torch.Tensor  # [1, H]
+
+    def c_struct(self) -> api.SharedExpert:
+        _need_cuda(self.gate_proj, self.up_proj, self.down_proj, self.gate_weight)
+        return api.SharedExpert(_ptr(self.gate_proj), _ptr(self.up_proj), _ptr(self.down_proj),
+                                _ptr(self.gate_weight))
+
+
+def _check_weights(w: ExpertWeights, H: int, dtype):
+    E, I = w.dims(H)
+    if w.kind == "dense":
+        if w.gate_up.dtype != dtype or w.down.dtype != dtype:
+            raise RuntimeError("dense expert weights must be in the activation dtype")
+        if tuple(w.gate_up.shape) != (E, 2 * I, H) or tuple(w.down.shape) != (E, H, I):
+            raise RuntimeError(f"expert weight shapes {tuple(w.gate_up.shape)} / "
+                               f"{tuple(w.down.shape)} do not match H={H}")
+    elif w.kind == "int4":
+        for t, (n, k) in ((w.gate_up, (2 * I, H)), (w.down, (H, I))):
+            if t.dtype not in (torch.int32, torch.uint8):
+                raise RuntimeError("int4 weights must be int32 or uint8 packed")
+            if t.shape[0] != E or t.shape[1] != n or t.numel() * t.element_size() != E * n * k // 2:
+                raise RuntimeError("int4 weight shape mismatch")
+        for s, n, k in ((w.gate_up_scale, 2 * I, H), (w.down_scale, H, I)):
+            if s is None or s.dtype != dtype:
+                raise RuntimeError("int4 scales must be given in the activation dtype")
+            want = E * n * (k // w.group if w.group else 1)
+            if s.numel() != want:
+                raise RuntimeError(f"int4 scale has {s.numel()} elements, expected {want}")
+    else:
+        raise RuntimeError(f"unknown weight kind {w.kind}")
+    return E, I
+
+
+def router_topk(h: torch.Tensor, w_r: torch.Tensor, top_k: int, bias: torch.Tensor | None = None,
+                return_logits: bool = False):
+    """``Qwen3_5MoeTopKRouter.forward`` on the device: ``(top_k_index int64, top_k_weights fp32)``.
+
+    Logits are correctly rounded model-dtype values of ``h @ w_r.T`` (+ ``bias``);
+    ties broken by ascending expert id.
+    """
+    _need_cuda(h, w_r, bias)
+    T, H = h.shape
+    E = w_r.shape[0]
+    if w_r.shape[1] != H or w_r.dtype != h.dtype or (bias is not None and bias.dtype != h.dtype):
+        raise RuntimeError("router weight / bias must match hidden size and dtype")
+    shape = _shape(T, H, E, 32, 0, top_k, h.dtype)
+    idx = torch.empty((T, top_k), dtype=torch.int64, device=h.device)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=h.device)
+    lg = torch.empty((T, E), dtype=torch.float32, device=h.device) if return_logits else None
+    L = api.lib()
+    nbytes = L.tarfa_b200_workspace_size(C.byref(shape), api.OP_ROUTER)
+    ws = workspace(nbytes, h.device)
+    api.check(L.tarfa_b200_router_topk(C.byref(shape), _ptr(h), _ptr(w_r), _ptr(bias), _ptr(idx),
+                                       _ptr(w), _ptr(lg), _ptr(ws), ws.numel(), _stream(h.device)))
+    return (idx, w, lg) if return_logits else (idx, w)
+
+
+def permute(top_idx: torch.Tensor, num_experts: int):
+    """Expert-sorted route order: ``(seg_offsets[E+1], perm_token[R], perm_slot[R])`` int32."""
+    _need_cuda(top_idx)
+    if top_idx.dtype != torch.int64:
+        raise RuntimeError("top_idx must be int64")
+    T, K = top_idx.shape
+    shape = _shape(T, 32, num_experts, 32, 0, K, torch.bfloat16)
+    dev = top_idx.device
+    seg = torch.zeros(num_experts + 1, dtype=torch.int32, device=dev)
+    tok = torch.empty(T * K, dtype=torch.int32, device=dev)
+    slot = torch.empty(T * K, dtype=torch.int32, device=dev)
+    L = api.lib()
+    ws = workspace(L.tarfa_b200_workspace_size(C.byref(shape), api.OP_PERMUTE), dev)
+    api.check(L.tarfa_b200_permute(C.byref(shape), _ptr(top_idx), _ptr(seg), _ptr(tok), _ptr(slot),
+                                   _ptr(ws), ws.numel(), _stream(dev)))
+    return seg, tok, slot
+
+
+def experts_forward(h: torch.Tensor, top_idx: torch.Tensor, top_w: torch.Tensor,
+                    weights: ExpertWeights, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The routed-experts closure: ``experts.forward(h, top_k_index, top_k_weights)``."""
+    _need_cuda(h, top_idx, top_w, out)
+    T, H = h.shape
+    if top_idx.dtype != torch.int64 or top_w.dtype != torch.float32 or top_idx.shape != top_w.shape:
+        raise RuntimeError("top_k_index int64 and top_k_weights fp32 of one shape [T, K]")
+    E, I = _check_weights(weights, H, h.dtype)
+    K = top_idx.shape[1]
+    if out is None:
+        out = torch.empty_like(h)
+    shape = _shape(T, H, E, I, 0, K, h.dtype)
+    L = api.lib()
+    ws = workspace(L.tarfa_b200_workspace_size(C.byref(shape), api.OP_EXPERTS), h.device)
+    wc = weights.c_struct()
+    api.check(L.tarfa_b200_experts_forward(C.byref(shape), _ptr(h), _ptr(top_idx), _ptr(top_w),
+                                           C.byref(wc), _ptr(out), _ptr(ws), ws.numel(),
+                                           _stream(h.device)))
+    return out
+
+
+def moe_layer(h: torch.Tensor, w_r: torch.Tensor, weights: ExpertWeights,
+              shared: SharedWeights | None, top_k: int = 8, bias: torch.Tensor | None = None,
+              return_routing: bool = False, out: torch.Tensor | None = None):
+    """``Qwen3_5MoeSparseMoeBlock.forward`` (router + routed experts + gated shared expert)."""
+    _need_cuda(h, w_r, bias, out)
+    T, H = h.shape
+    E, I = _check_weights(weights, H, h.dtype)
+    if w_r.shape != (E, H) or w_r.dtype != h.dtype:
+        raise RuntimeError("router weight must be [E, H] in the activation dtype")
+    Is = shared.gate_proj.shape[0] if shared is not None else 0
+    if out is None:
+        out = torch.empty_like(h)
+    idx = torch.empty((T, top_k), dtype=torch.int64, device=h.device) if return_routing else None
+    wt = torch.empty((T, top_k), dtype=torch.float32, device=h.device) if return_routing else None
+    shape = _shape(T, H, E, I, Is, top_k, h.dtype)
+    L = api.lib()
+    ws = workspace(L.tarfa_b200_workspace_size(C.byref(shape), api.OP_MOE_LAYER), h.device)
+    wc = weights.c_struct()
+    sc = shared.c_struct() if shared is not None else None
+    api.check(L.tarfa_b200_moe_layer(C.byref(shape), _ptr(h), _ptr(w_r), _ptr(bias), C.byref(wc),
+                                     C.byref(sc) if sc is not None else None, _ptr(out), _ptr(idx),
+                                     _ptr(wt), _ptr(ws), ws.numel(), _stream(h.device)))
+    return (out, idx, wt) if return_routing else out
+
+
+def dequant_int4(packed: torch.Tensor, scale: torch.Tensor, group: int = 0) -> torch.Tensor:
+    """``channel_q4.dequant_int4`` on the device (group 0 = one scale per row)."""
+    _need_cuda(packed, scale)
+    N = packed.shape[0]
+    K = packed.numel() * packed.element_size() * 2 // N
+    out = torch.empty((N, K), dtype=scale.dtype, device=packed.device)
+    api.check(api.lib().tarfa_b200_dequant_int4(_ptr(packed), _ptr(scale), N, K, group,
+                                                _DT[scale.dtype], _ptr(out), _stream(packed.device)))
+    return out
+
+
+def quantize_int4(w: torch.Tensor, group: int = 128):
+    """Symmetric int4 quantisation of bf16 ``w [N, K]`` -> (int32 ``[N, K/8]``, bf16 ``[N, K/group]``)."""
+    _need_cuda(w)
+    if w.dtype != torch.bfloat16:
+        raise RuntimeError("quantize_int4 takes bf16 weights")
+    N, K = w.shape[-2], w.shape[-1]
+    lead = w.shape[:-2]
+    rows = w.numel() // K
+    packed = torch.empty((*lead, N, K // 8), dtype=torch.int32, device=w.device)
+    scale = torch.empty((*lead, N, K // group), dtype=torch.bfloat16, device=w.device)
+    api.check(api.lib().tarfa_b200_quantize_int4(_ptr(w), rows, K, group, _ptr(packed), _ptr(scale),
+                                                 _stream(w.device)))
+    return packed, scale
+
+
+def set_stage_events(events) -> None:
+    """Record ``events[i]`` (``torch.cuda.Event``) at layer stage boundary ``i``
+    (0 start, 1 router/permute, 2 gate_up, 3 down, 4 combine) on this thread;
+    ``None`` or ``[]`` turns it off.  Each event must have been recorded once."""
+    events = list(events or [])
+    arr = (C.c_void_p * max(1, len(events)))(*[C.c_void_p(e.cuda_event) for e in events])
+    api.check(api.lib().tarfa_b200_set_stage_events(arr, len(events)))
+
+
+def device_status(clear: bool = False) -> int:
+    """Error bits raised by kernels on the current device (``DEV_*`` in ``_capi``)."""
+    v = C.c_uint32(0)
+    api.check(api.lib().tarfa_b200_device_status(C.byref(v), int(clear),
+                                                 _stream(torch.cuda.current_device())))
+    return v.value
