@@ -203,9 +203,24 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
         const int n_it = K / 128;
         const int i0 = kw * n_it / KSPLIT, i1 = (kw + 1) * n_it / KSPLIT;
         const bool grp_scale = a.group != 0;
-        for (int it = i0; it < i1; ++it) {
-          const int64_t woff = ((int64_t)it * 16 + c * 4) * 4;   // bytes
-          const uint4 qa = ld_stream(rowA + woff), qb = ld_stream(rowB + woff);
+        constexpr int NBQ = 4;   // iterations whose weights are in flight together
+        for (int ib = i0; ib < i1; ib += NBQ) {
+          uint4 qa_b[NBQ], qb_b[NBQ];
+#pragma unroll
+          for (int j = 0; j < NBQ; ++j) {
+            qa_b[j] = make_uint4(0, 0, 0, 0);
+            qb_b[j] = qa_b[j];
+            if (ib + j < i1) {
+              const int64_t woff = ((int64_t)(ib + j) * 16 + c * 4) * 4;   // bytes
+              qa_b[j] = ld_stream(rowA + woff);
+              qb_b[j] = ld_stream(rowB + woff);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < NBQ; ++j) {
+          const int it = ib + j;
+          if (it >= i1) break;
+          const uint4 qa = qa_b[j], qb = qb_b[j];
           float sa = 1.f, sb = 1.f;
           uint32_t sa2 = 0, sb2 = 0;
           if (grp_scale || MODE == kModeInt4Dequant) {
@@ -263,6 +278,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
               acc[b][2] = fmaf(part[b][2], sb, acc[b][2]);
               acc[b][3] = fmaf(part[b][3], sb, acc[b][3]);
             }
+          }
           }
         }
       }

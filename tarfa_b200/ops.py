@@ -224,6 +224,57 @@ def moe_layer(h: torch.Tensor, w_r: torch.Tensor, weights: ExpertWeights,
     return (out, idx, wt) if return_routing else out
 
 
+class MoePlan:
+    """A prepared ``moe_layer`` call on fixed device buffers.
+
+    Shapes, pointers and the C structs are built once; :meth:`run` is a single
+    foreign call (a few microseconds of host time), and :meth:`capture`
+    records the layer's kernels into a CUDA graph so a decode step replays
+    them with no host launch work at all.  The plan owns a private workspace,
+    so plans may run on different streams.  Inputs are read from ``self.h``
+    (copy new tokens into it), the result lands in ``self.out``.
+    """
+
+    def __init__(self, h: torch.Tensor, w_r: torch.Tensor, weights: ExpertWeights,
+                 shared: SharedWeights | None, top_k: int = 8, bias: torch.Tensor | None = None,
+                 return_routing: bool = False):
+        _need_cuda(h, w_r, bias)
+        T, H = h.shape
+        E, I = _check_weights(weights, H, h.dtype)
+        if w_r.shape != (E, H) or w_r.dtype != h.dtype:
+            raise RuntimeError("router weight must be [E, H] in the activation dtype")
+        Is = shared.gate_proj.shape[0] if shared is not None else 0
+        self.h, self.w_r, self.bias, self.weights, self.shared = h, w_r, bias, weights, shared
+        self.out = torch.empty_like(h)
+        dev = h.device
+        self.top_idx = torch.empty((T, top_k), dtype=torch.int64, device=dev) if return_routing else None
+        self.top_w = torch.empty((T, top_k), dtype=torch.float32, device=dev) if return_routing else None
+        self._shape = _shape(T, H, E, I, Is, top_k, h.dtype)
+        L = api.lib()
+        n = L.tarfa_b200_workspace_size(C.byref(self._shape), api.OP_MOE_LAYER)
+        self.ws = torch.zeros(n, dtype=torch.uint8, device=dev)
+        self._wc = weights.c_struct()
+        self._sc = shared.c_struct() if shared is not None else None
+        self._fn = L.tarfa_b200_moe_layer
+        self._args = (C.byref(self._shape), _ptr(h), _ptr(w_r), _ptr(bias), C.byref(self._wc),
+                      C.byref(self._sc) if self._sc is not None else None, _ptr(self.out),
+                      _ptr(self.top_idx), _ptr(self.top_w), _ptr(self.ws), C.c_size_t(n))
+        self.device = dev
+
+    def run(self) -> torch.Tensor:
+        api.check(self._fn(*self._args, C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
+        return self.out
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """Record the layer into a CUDA graph (after one eager warm-up run)."""
+        self.run()
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.run()
+        return g
+
+
 def dequant_int4(packed: torch.Tensor, scale: torch.Tensor, group: int = 0) -> torch.Tensor:
     """``channel_q4.dequant_int4`` on the device (group 0 = one scale per row)."""
     _need_cuda(packed, scale)
