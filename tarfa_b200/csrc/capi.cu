@@ -8,7 +8,10 @@
 #include <string>
 
 #include "../../include/tarfa_b200.h"
+#include <atomic>
+
 #include "common.cuh"
+#include "gemm_sm100.h"
 #include "gemv.cuh"
 #include "int4.cuh"
 #include "router.cuh"
@@ -83,7 +86,8 @@ int device_info(unsigned** status, int* sms) {
 // workspace layout
 // ---------------------------------------------------------------------------
 struct Ws {
-  size_t counter, logits, gate_logit, idx32, topw, units, perm_tok, perm_slot, route_row, act, y;
+  size_t counter, logits, gate_logit, idx32, topw, units, perm_tok, perm_slot, route_row, act, y,
+      xperm;
   size_t total;
 };
 
@@ -113,6 +117,7 @@ Ws layout(const tarfa_moe_shape& s, int op) {
   if (op == TARFA_OP_MOE_LAYER || op == TARFA_OP_EXPERTS) {
     w.act = take(Rt * Imax * 2);
     w.y = take(Rt * H * 4);
+    w.xperm = take(Rt * H * 2);
   }
   w.total = o;
   return w;
@@ -185,6 +190,15 @@ int launch_gemv_ntb(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStrea
 constexpr int kKsplitGateUp = 8;
 constexpr int kKsplitDown = 4;
 
+// Token count from which dense layers take the tcgen05 grouped-GEMM path
+// (tarfa_b200_set_gemm_min_tokens); below it the tensor-core GEMV path.
+std::atomic<int64_t> g_gemm_min_tokens{64};
+
+bool use_gemm(const tarfa_moe_shape& s, const tarfa_moe_weights& w, int64_t Is) {
+  return w.kind == TARFA_W_DENSE && s.tokens >= g_gemm_min_tokens.load() &&
+         prefill_supported(s.hidden, s.inter, Is, true);
+}
+
 template <typename T>
 int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_weights& w,
                 const tarfa_shared_expert* sh, const Ws& L, void* ws, void* out,
@@ -197,6 +211,39 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
   const bool int4 = w.kind == TARFA_W_INT4;
   const int mode = !int4 ? kModeExact : (T_ == 1 ? kModeInt4Fused : kModeInt4Dequant);
   int32_t* units = at<int32_t>(ws, L.units);
+
+  if (use_gemm(s, w, Is)) {   // batched / prefill: tcgen05 grouped GEMM over the segments
+    PrefillArgs p{};
+    p.bf16 = s.dtype == TARFA_BF16;
+    p.T = T_;
+    p.H = H;
+    p.E = E;
+    p.E_store = E;
+    p.I = I;
+    p.Is = Is;
+    p.rows_total = R + (Is ? T_ : 0);
+    p.max_units = Umax + 1;
+    p.hidden = hidden;
+    p.perm_tok = at<int32_t>(ws, L.perm_tok);
+    p.units = units;
+    p.expert_slot = w.expert_slot;
+    p.gate_up = w.gate_up;
+    p.down = w.down;
+    p.sh_gate = sh ? sh->gate_proj : nullptr;
+    p.sh_up = sh ? sh->up_proj : nullptr;
+    p.sh_down = sh ? sh->down_proj : nullptr;
+    p.x_perm = at<void>(ws, L.xperm);
+    p.act = at<void>(ws, L.act);
+    p.ld_act = Imax;
+    p.y = at<void>(ws, L.y);
+    p.status = status;
+    p.sms = sms;
+    const char* err = nullptr;
+    if (prefill_experts_sm100(p, st, &err)) return fail(TARFA_ERR_CUDA, "%s", err ? err : "prefill");
+    stage_mark(2, st);
+    stage_mark(3, st);
+    return TARFA_OK;
+  }
 
   GemvArgs g{};
   g.units = units;
@@ -290,10 +337,10 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
 
 template <typename T>
 int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* top_w, bool int4,
-                bool with_shared, void* out, cudaStream_t st) {
+                bool with_shared, bool gemm_y, void* out, cudaStream_t st) {
   const int T_ = (int)s.tokens, K = s.top_k, H = (int)s.hidden;
   CombineArgs c{};
-  c.y = at<float>(ws, L.y);
+  c.y = at<void>(ws, L.y);
   c.route_row = at<int32_t>(ws, L.route_row);
   c.idx32 = at<int32_t>(ws, L.idx32);
   c.w = top_w;
@@ -307,7 +354,8 @@ int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* to
   c.gate_logit = with_shared ? at<float>(ws, L.gate_logit) : nullptr;
   c.out = out;
   dim3 grid((H + 255) / 256, T_);
-  combine_kernel<T><<<grid, 256, 0, st>>>(c);
+  if (gemm_y) combine_kernel<T, T><<<grid, 256, 0, st>>>(c);   // GEMM path: y in the model dtype
+  else combine_kernel<T, float><<<grid, 256, 0, st>>>(c);
   TARFA_CUDA(cudaGetLastError());
   stage_mark(4, st);
   return TARFA_OK;
@@ -391,6 +439,12 @@ const char* tarfa_b200_last_error(void) { return g_last_error.c_str(); }
 size_t tarfa_b200_workspace_size(const tarfa_moe_shape* shape, int32_t op) {
   if (!shape) return 0;
   return layout(*shape, op).total;
+}
+
+int tarfa_b200_set_gemm_min_tokens(int64_t tokens) {
+  if (tokens < 1) return fail(TARFA_ERR_INVALID, "gemm_min_tokens %lld < 1", (long long)tokens);
+  g_gemm_min_tokens.store(tokens);
+  return TARFA_OK;
 }
 
 int tarfa_b200_set_stage_events(void* const* events, int32_t n) {
@@ -486,10 +540,10 @@ int tarfa_b200_experts_forward(const tarfa_moe_shape* shape, const void* hidden,
   int rc;
   if (shape->dtype == TARFA_BF16) {
     rc = run_experts<__nv_bfloat16>(*shape, hidden, *weights, nullptr, L, workspace, out, status, sms, st);
-    if (!rc) rc = run_combine<__nv_bfloat16>(*shape, L, workspace, top_w, int4, false, out, st);
+    if (!rc) rc = run_combine<__nv_bfloat16>(*shape, L, workspace, top_w, int4, false, use_gemm(*shape, *weights, 0), out, st);
   } else {
     rc = run_experts<__half>(*shape, hidden, *weights, nullptr, L, workspace, out, status, sms, st);
-    if (!rc) rc = run_combine<__half>(*shape, L, workspace, top_w, int4, false, out, st);
+    if (!rc) rc = run_combine<__half>(*shape, L, workspace, top_w, int4, false, use_gemm(*shape, *weights, 0), out, st);
   }
   return rc;
 }
@@ -532,14 +586,14 @@ int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
                                       top_w_out, nullptr, true, sh != nullptr, status, st);
     if (!rc) stage_mark(1, st);
     if (!rc) rc = run_experts<__nv_bfloat16>(s, hidden, *weights, sh, L, workspace, out, status, sms, st);
-    if (!rc) rc = run_combine<__nv_bfloat16>(s, L, workspace, at<float>(workspace, L.topw), int4, sh != nullptr, out, st);
+    if (!rc) rc = run_combine<__nv_bfloat16>(s, L, workspace, at<float>(workspace, L.topw), int4, sh != nullptr, use_gemm(s, *weights, s.shared_inter), out, st);
   } else {
     rc = launch_router<__half>(s, hidden, router_weight, router_bias,
                                sh ? sh->gate_weight : nullptr, L, workspace, top_idx_out,
                                top_w_out, nullptr, true, sh != nullptr, status, st);
     if (!rc) stage_mark(1, st);
     if (!rc) rc = run_experts<__half>(s, hidden, *weights, sh, L, workspace, out, status, sms, st);
-    if (!rc) rc = run_combine<__half>(s, L, workspace, at<float>(workspace, L.topw), int4, sh != nullptr, out, st);
+    if (!rc) rc = run_combine<__half>(s, L, workspace, at<float>(workspace, L.topw), int4, sh != nullptr, use_gemm(s, *weights, s.shared_inter), out, st);
   }
   return rc;
 }

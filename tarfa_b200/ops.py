@@ -301,6 +301,12 @@ def quantize_int4(w: torch.Tensor, group: int = 128):
     return packed, scale
 
 
+def set_gemm_min_tokens(tokens: int) -> None:
+    """Dense layers with at least ``tokens`` tokens take the tcgen05 grouped-GEMM
+    path; fewer take the tensor-core GEMV path (process-wide, default 64)."""
+    api.check(api.lib().tarfa_b200_set_gemm_min_tokens(int(tokens)))
+
+
 def set_stage_events(events) -> None:
     """Record ``events[i]`` (``torch.cuda.Event``) at layer stage boundary ``i``
     (0 start, 1 router/permute, 2 gate_up, 3 down, 4 combine) on this thread;
