@@ -48,6 +48,9 @@ SIGNATURES = {
                                              C.POINTER(MoeWeights), _P, _P, C.c_size_t, _P]),
     "tarfa_b200_moe_layer": (C.c_int, [C.POINTER(MoeShape), _P, _P, _P, C.POINTER(MoeWeights),
                                        C.POINTER(SharedExpert), _P, _P, _P, _P, C.c_size_t, _P]),
+    "tarfa_b200_moe_layer_noalloc": (C.c_int, [C.POINTER(MoeShape), _P, _P, _P,
+                                               C.POINTER(MoeWeights), C.POINTER(SharedExpert),
+                                               _P, _P, _P, _P]),
     "tarfa_b200_router_topk": (C.c_int, [C.POINTER(MoeShape), _P, _P, _P, _P, _P, _P, _P,
                                          C.c_size_t, _P]),
     "tarfa_b200_permute": (C.c_int, [C.POINTER(MoeShape), _P, _P, _P, _P, _P, C.c_size_t, _P]),

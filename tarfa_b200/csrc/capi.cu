@@ -83,6 +83,32 @@ int device_info(unsigned** status, int* sms) {
 }
 
 // ---------------------------------------------------------------------------
+// static scratch of tarfa_b200_moe_layer_noalloc: a file-scope device array.
+// In host code the symbol is only a host-side stand-in; its device address is
+// looked up once per device (with that device current) and cached.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = TARFA_B200_NOALLOC_SCRATCH_BYTES;
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+void* g_noalloc_ptr[kMaxDevices];
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  TARFA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TARFA_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(TARFA_ERR_CUDA, "cudaGetSymbolAddress(noalloc scratch) failed: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TARFA_OK;
+}
+
+// ---------------------------------------------------------------------------
 // workspace layout
 // ---------------------------------------------------------------------------
 struct Ws {
@@ -596,6 +622,31 @@ int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
     if (!rc) rc = run_combine<__half>(s, L, workspace, at<float>(workspace, L.topw), int4, sh != nullptr, use_gemm(s, *weights, s.shared_inter), out, st);
   }
   return rc;
+}
+
+// The whole layer with the library's own static scratch instead of a
+// caller-supplied workspace (see the header for who needs this and the rules).
+int tarfa_b200_moe_layer_noalloc(const tarfa_moe_shape* shape, const void* hidden,
+                                 const void* router_weight, const void* router_bias,
+                                 const tarfa_moe_weights* weights,
+                                 const tarfa_shared_expert* shared, void* out,
+                                 int64_t* top_idx_out, float* top_w_out, void* stream) {
+  if (int rc = check_shape(shape)) return rc;
+  tarfa_moe_shape s = *shape;
+  if (!(shared && shape->shared_inter > 0)) s.shared_inter = 0;
+  const Ws L = layout(s, TARFA_OP_MOE_LAYER);
+  if (L.total > kNoAllocScratchBytes)
+    return fail(TARFA_ERR_UNSUPPORTED,
+                "moe_layer_noalloc: this shape needs %zu bytes of scratch; the static scratch "
+                "holds %zu bytes (use tarfa_b200_moe_layer with a workspace)",
+                L.total, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the router's completion counter must start at zero, whatever the last call left
+  TARFA_CUDA(cudaMemsetAsync(at<char>(scratch, L.counter), 0, 16, st));
+  return tarfa_b200_moe_layer(shape, hidden, router_weight, router_bias, weights, shared, out,
+                              top_idx_out, top_w_out, scratch, kNoAllocScratchBytes, stream);
 }
 
 int tarfa_b200_dequant_int4(const int32_t* packed, const void* scale, int64_t rows, int64_t cols,
