@@ -60,6 +60,7 @@ SIGNATURES = {
     "tarfa_b200_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int32, _P]),
     "tarfa_b200_set_stage_events": (C.c_int, [C.POINTER(C.c_void_p), C.c_int32]),
     "tarfa_b200_set_gemm_min_tokens": (C.c_int, [C.c_int64]),
+    "tarfa_b200_set_fused_decode_max_tokens": (C.c_int, [C.c_int64]),
 }
 
 _lock = threading.Lock()

@@ -15,6 +15,7 @@
 #include "gemv.cuh"
 #include "int4.cuh"
 #include "router.cuh"
+#include "decode_fused.cuh"
 
 using namespace tarfa;
 
@@ -113,11 +114,13 @@ int noalloc_scratch(void** out) {
 // ---------------------------------------------------------------------------
 struct Ws {
   size_t counter, logits, gate_logit, idx32, topw, units, perm_tok, perm_slot, route_row, act, y,
-      xperm;
+      xperm, bar, hb_cnt;
   size_t total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+constexpr size_t kZeroHeaderBytes = 2304;   // 16 + 16 + 8192/16*4, rounded to 256
 
 Ws layout(const tarfa_moe_shape& s, int op) {
   const int64_t T = s.tokens, K = s.top_k, E = s.experts, H = s.hidden;
@@ -129,7 +132,12 @@ Ws layout(const tarfa_moe_shape& s, int op) {
   Ws w{};
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o += align256(bytes); return at; };
-  w.counter = take(16);
+  // Header shared by every op: counters that every kernel leaves at zero.
+  // Identical offsets for all ops, so one workspace can serve any sequence of calls.
+  w.counter = 0;
+  w.bar = 16;
+  w.hb_cnt = 32;   // 8192 / 16 counters at most (hidden <= 8192)
+  o = kZeroHeaderBytes;
   w.units = take((4 + 4 * Umax) * 4);
   w.idx32 = take(R * 4);
   w.topw = take(R * 4);
@@ -223,6 +231,79 @@ std::atomic<int64_t> g_gemm_min_tokens{64};
 bool use_gemm(const tarfa_moe_shape& s, const tarfa_moe_weights& w, int64_t Is) {
   return w.kind == TARFA_W_DENSE && s.tokens >= g_gemm_min_tokens.load() &&
          prefill_supported(s.hidden, s.inter, Is, true);
+}
+
+// Largest batch that takes the fused single-launch decode kernel (0: never).
+std::atomic<int64_t> g_fused_max_tokens{fused::kMaxT};
+
+bool use_fused_decode(const tarfa_moe_shape& s, const tarfa_moe_weights& w) {
+  return s.tokens >= 1 && s.tokens <= g_fused_max_tokens.load() && s.tokens <= fused::kMaxT &&
+         s.top_k <= fused::kMaxK && !use_gemm(s, w, s.shared_inter) && s.hidden % 16 == 0;
+}
+
+template <typename T>
+int launch_fused(const tarfa_moe_shape& s, const void* hidden, const void* w_r, const void* bias,
+                 const tarfa_moe_weights& w, const tarfa_shared_expert* sh, void* out,
+                 int64_t* idx_out, float* w_out, const Ws& L, void* ws, unsigned* status, int sms,
+                 cudaStream_t st) {
+  fused::Args a{};
+  a.T = (int)s.tokens;
+  a.H = (int)s.hidden;
+  a.E = (int)s.experts;
+  a.K = s.top_k;
+  a.I = (int)s.inter;
+  a.Is = sh ? (int)s.shared_inter : 0;
+  a.Imax = a.I > a.Is ? a.I : a.Is;
+  a.group = w.group;
+  a.h = hidden;
+  a.w_r = w_r;
+  a.bias = bias;
+  a.w_sg = sh ? sh->gate_weight : nullptr;
+  a.gate_up = w.gate_up;
+  a.down = w.down;
+  a.gu_scale = w.gate_up_scale;
+  a.dn_scale = w.down_scale;
+  a.expert_slot = w.expert_slot;
+  a.sh_gate = sh ? sh->gate_proj : nullptr;
+  a.sh_up = sh ? sh->up_proj : nullptr;
+  a.sh_down = sh ? sh->down_proj : nullptr;
+  a.out = out;
+  a.idx_out = idx_out;
+  a.w_out = w_out;
+  a.logits = at<float>(ws, L.logits);
+  a.gate_logit = at<float>(ws, L.gate_logit);
+  a.act = at<void>(ws, L.act);
+  a.y = at<float>(ws, L.y);
+  a.bar = at<unsigned>(ws, L.bar);
+  a.hb_cnt = at<unsigned>(ws, L.hb_cnt);
+  a.status = status;
+  const bool int4 = w.kind == TARFA_W_INT4;
+  const int mode = !int4 ? kModeExact : (a.T == 1 ? kModeInt4Fused : kModeInt4Dequant);
+  void (*kern)(const fused::Args);
+  if (a.T <= 8) {
+    kern = mode == kModeExact        ? fused::decode_layer_kernel<T, kModeExact, 1>
+           : mode == kModeInt4Fused ? fused::decode_layer_kernel<T, kModeInt4Fused, 1>
+                                    : fused::decode_layer_kernel<T, kModeInt4Dequant, 1>;
+  } else {
+    kern = mode == kModeExact        ? fused::decode_layer_kernel<T, kModeExact, 2>
+           : mode == kModeInt4Fused ? fused::decode_layer_kernel<T, kModeInt4Fused, 2>
+                                    : fused::decode_layer_kernel<T, kModeInt4Dequant, 2>;
+  }
+  int per_sm = 0;
+  TARFA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, fused::kThreads, 0));
+  if (per_sm < 1) return fail(TARFA_ERR_UNSUPPORTED, "fused decode kernel does not fit an SM");
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(sms);          // one CTA per SM, all co-resident (cooperative)
+  cfg.blockDim = dim3(fused::kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TARFA_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  return TARFA_OK;
 }
 
 template <typename T>
@@ -467,6 +548,12 @@ size_t tarfa_b200_workspace_size(const tarfa_moe_shape* shape, int32_t op) {
   return layout(*shape, op).total;
 }
 
+int tarfa_b200_set_fused_decode_max_tokens(int64_t tokens) {
+  if (tokens < 0) return fail(TARFA_ERR_INVALID, "fused_decode_max_tokens %lld < 0", (long long)tokens);
+  g_fused_max_tokens.store(tokens);
+  return TARFA_OK;
+}
+
 int tarfa_b200_set_gemm_min_tokens(int64_t tokens) {
   if (tokens < 1) return fail(TARFA_ERR_INVALID, "gemm_min_tokens %lld < 1", (long long)tokens);
   g_gemm_min_tokens.store(tokens);
@@ -606,6 +693,15 @@ int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
   const tarfa_shared_expert* sh = has_shared ? shared : nullptr;
   int rc;
   stage_mark(0, st);
+  if (use_fused_decode(s, *weights)) {   // decode batch: one persistent cooperative launch
+    rc = s.dtype == TARFA_BF16
+             ? launch_fused<__nv_bfloat16>(s, hidden, router_weight, router_bias, *weights, sh, out,
+                                           top_idx_out, top_w_out, L, workspace, status, sms, st)
+             : launch_fused<__half>(s, hidden, router_weight, router_bias, *weights, sh, out,
+                                    top_idx_out, top_w_out, L, workspace, status, sms, st);
+    if (!rc) stage_mark(4, st);
+    return rc;
+  }
   if (s.dtype == TARFA_BF16) {
     rc = launch_router<__nv_bfloat16>(s, hidden, router_weight, router_bias,
                                       sh ? sh->gate_weight : nullptr, L, workspace, top_idx_out,
@@ -643,8 +739,9 @@ int tarfa_b200_moe_layer_noalloc(const tarfa_moe_shape* shape, const void* hidde
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // the router's completion counter must start at zero, whatever the last call left
-  TARFA_CUDA(cudaMemsetAsync(at<char>(scratch, L.counter), 0, 16, st));
+  // the kernels' counters (router completion, grid barrier, per-block completion)
+  // must start at zero, whatever the last call left
+  TARFA_CUDA(cudaMemsetAsync(scratch, 0, kZeroHeaderBytes, st));
   return tarfa_b200_moe_layer(shape, hidden, router_weight, router_bias, weights, shared, out,
                               top_idx_out, top_w_out, scratch, kNoAllocScratchBytes, stream);
 }

@@ -76,6 +76,153 @@ TARFA_DEVI void group_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// One warp's share of a 16-row tile: acc[b] += W(rows g, g+8)[k in iterations
+// [i0, i1)] . x(token block b).  An iteration is 32 k (dense) or 128 k (int4,
+// one scale group).  xrow[b] is this lane's token row (null: zero column).
+// Dense weights are double-buffered in registers: the next 4 iterations'
+// loads are in flight while the current ones feed the tensor cores.
+template <typename T, int MODE, int NTB>
+TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, const T* scB,
+                           int group, int i0, int i1, const char* const (&xrow)[NTB],
+                           float (&acc)[NTB][4]) {
+  const int c = (threadIdx.x & 31) & 3;
+  if (MODE == kModeExact) {
+    constexpr int NB = 4;
+    uint4 wa[NB], wb[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      wa[j] = make_uint4(0, 0, 0, 0);
+      wb[j] = wa[j];
+      if (i0 + j < i1) {
+        const int64_t off = ((int64_t)(i0 + j) * 32 + c * 8) * (int64_t)sizeof(T);
+        wa[j] = ld_stream(rowA + off);
+        wb[j] = ld_stream(rowB + off);
+      }
+    }
+    for (int it = i0; it < i1; it += NB) {
+      uint4 na[NB], nb[NB];
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        na[j] = make_uint4(0, 0, 0, 0);
+        nb[j] = na[j];
+        if (it + NB + j < i1) {
+          const int64_t off = ((int64_t)(it + NB + j) * 32 + c * 8) * (int64_t)sizeof(T);
+          na[j] = ld_stream(rowA + off);
+          nb[j] = ld_stream(rowB + off);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        if (it + j < i1) {
+          const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
+#pragma unroll
+          for (int b = 0; b < NTB; ++b) {
+            uint4 xv = make_uint4(0, 0, 0, 0);
+            if (xrow[b]) xv = ld_cached(xrow[b] + off);
+            Mma<T>::run(acc[b], wa[j].x, wb[j].x, wa[j].y, wb[j].y, xv.x, xv.y);
+            Mma<T>::run(acc[b], wa[j].z, wb[j].z, wa[j].w, wb[j].w, xv.z, xv.w);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        wa[j] = na[j];
+        wb[j] = nb[j];
+      }
+    }
+  } else {
+    // lane c covers k [32c, 32c+32) of each 128-k iteration
+    const bool grp_scale = group != 0;
+    constexpr int NBQ = 4;   // iterations whose weights are in flight together
+    for (int ib = i0; ib < i1; ib += NBQ) {
+      uint4 qa_b[NBQ], qb_b[NBQ];
+#pragma unroll
+      for (int j = 0; j < NBQ; ++j) {
+        qa_b[j] = make_uint4(0, 0, 0, 0);
+        qb_b[j] = qa_b[j];
+        if (ib + j < i1) {
+          const int64_t woff = ((int64_t)(ib + j) * 16 + c * 4) * 4;   // bytes
+          qa_b[j] = ld_stream(rowA + woff);
+          qb_b[j] = ld_stream(rowB + woff);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NBQ; ++j) {
+        const int it = ib + j;
+        if (it >= i1) break;
+        const uint4 qa = qa_b[j], qb = qb_b[j];
+        float sa = 1.f, sb = 1.f;
+        uint32_t sa2 = 0, sb2 = 0;
+        if (grp_scale || MODE == kModeInt4Dequant) {
+          const int gi = grp_scale ? (it * 128) / group : 0;
+          const uint16_t ua = reinterpret_cast<const uint16_t*>(scA)[gi];
+          const uint16_t ub = reinterpret_cast<const uint16_t*>(scB)[gi];
+          sa = Elem<T>::bits_to_f(ua);
+          sb = Elem<T>::bits_to_f(ub);
+          sa2 = uint32_t(ua) | (uint32_t(ua) << 16);
+          sb2 = uint32_t(ub) | (uint32_t(ub) << 16);
+        }
+        float part[NTB][4];
+#pragma unroll
+        for (int b = 0; b < NTB; ++b)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) part[b][q] = 0.f;
+        const uint32_t qaw[4] = {qa.x, qa.y, qa.z, qa.w};
+        const uint32_t qbw[4] = {qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          uint32_t pa[4], pb[4];
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+            pa[s] = nib_pair<T>(qaw[m], s);
+            pb[s] = nib_pair<T>(qbw[m], s);
+            if (MODE == kModeInt4Dequant) {
+              pa[s] = Mma<T>::mul2(pa[s], sa2);
+              pb[s] = Mma<T>::mul2(pb[s], sb2);
+            }
+          }
+          const int64_t xoff = ((int64_t)it * 128 + c * 32 + m * 8) * (int64_t)sizeof(T);
+#pragma unroll
+          for (int b = 0; b < NTB; ++b) {
+            uint4 xv = make_uint4(0, 0, 0, 0);
+            if (xrow[b]) xv = ld_cached(xrow[b] + xoff);
+            // (x0,x4) (x1,x5) (x2,x6) (x3,x7) to match nibble pairs (s, s+4)
+            const uint32_t x04 = __byte_perm(xv.x, xv.z, 0x5410);
+            const uint32_t x15 = __byte_perm(xv.x, xv.z, 0x7632);
+            const uint32_t x26 = __byte_perm(xv.y, xv.w, 0x5410);
+            const uint32_t x37 = __byte_perm(xv.y, xv.w, 0x7632);
+            if (MODE == kModeInt4Fused && grp_scale) {
+              Mma<T>::run(part[b], pa[0], pb[0], pa[1], pb[1], x04, x15);
+              Mma<T>::run(part[b], pa[2], pb[2], pa[3], pb[3], x26, x37);
+            } else {
+              Mma<T>::run(acc[b], pa[0], pb[0], pa[1], pb[1], x04, x15);
+              Mma<T>::run(acc[b], pa[2], pb[2], pa[3], pb[3], x26, x37);
+            }
+          }
+        }
+        if (MODE == kModeInt4Fused && grp_scale) {
+#pragma unroll
+          for (int b = 0; b < NTB; ++b) {
+            acc[b][0] = fmaf(part[b][0], sa, acc[b][0]);
+            acc[b][1] = fmaf(part[b][1], sa, acc[b][1]);
+            acc[b][2] = fmaf(part[b][2], sb, acc[b][2]);
+            acc[b][3] = fmaf(part[b][3], sb, acc[b][3]);
+          }
+        }
+      }
+    }
+  }
+}
+
+// Epilogue value of one (row, token) pair of a tile, per mode:
+// GATE_UP: act from (gate, up); DOWN: y (model-dtype value, or fp32 for the fused int4 decode).
+template <typename T, int MODE>
+TARFA_DEVI float gate_up_act(float g, float u) {
+  if (MODE == kModeInt4Fused) return silu_f(g) * u;          // moe_kernel.py:99-100
+  const float gr = rnd<T>(g), ur = rnd<T>(u);                // fused_int4.py:193 / 242
+  return rnd<T>(silu_f(gr)) * ur;
+}
+
 template <typename T, int MODE, int PHASE, int KSPLIT, int NTB>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a) {
   constexpr bool INT4 = MODE != kModeExact;
@@ -162,125 +309,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
         }
       }
 
-      if (!INT4) {
-        const int n_it = K / 32;
+      {
+        const int n_it = K / (INT4 ? 128 : 32);
         const int i0 = kw * n_it / KSPLIT, i1 = (kw + 1) * n_it / KSPLIT;
-        int it = i0;
-        constexpr int NB = 4;
-        for (; it + NB <= i1; it += NB) {
-          uint4 wa[NB], wb2[NB];
-#pragma unroll
-          for (int j = 0; j < NB; ++j) {
-            const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
-            wa[j] = ld_stream(rowA + off);
-            wb2[j] = ld_stream(rowB + off);
-          }
-#pragma unroll
-          for (int j = 0; j < NB; ++j) {
-            const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
-#pragma unroll
-            for (int b = 0; b < NTB; ++b) {
-              uint4 xv = make_uint4(0, 0, 0, 0);
-              if (xrow[b]) xv = ld_cached(xrow[b] + off);
-              Mma<T>::run(acc[b], wa[j].x, wb2[j].x, wa[j].y, wb2[j].y, xv.x, xv.y);
-              Mma<T>::run(acc[b], wa[j].z, wb2[j].z, wa[j].w, wb2[j].w, xv.z, xv.w);
-            }
-          }
-        }
-        for (; it < i1; ++it) {
-          const int64_t off = ((int64_t)it * 32 + c * 8) * (int64_t)sizeof(T);
-          const uint4 wa = ld_stream(rowA + off), wb2 = ld_stream(rowB + off);
-#pragma unroll
-          for (int b = 0; b < NTB; ++b) {
-            uint4 xv = make_uint4(0, 0, 0, 0);
-            if (xrow[b]) xv = ld_cached(xrow[b] + off);
-            Mma<T>::run(acc[b], wa.x, wb2.x, wa.y, wb2.y, xv.x, xv.y);
-            Mma<T>::run(acc[b], wa.z, wb2.z, wa.w, wb2.w, xv.z, xv.w);
-          }
-        }
-      } else {
-        // one iteration = 128 k; lane c covers k [32c, 32c+32) of it
-        const int n_it = K / 128;
-        const int i0 = kw * n_it / KSPLIT, i1 = (kw + 1) * n_it / KSPLIT;
-        const bool grp_scale = a.group != 0;
-        constexpr int NBQ = 4;   // iterations whose weights are in flight together
-        for (int ib = i0; ib < i1; ib += NBQ) {
-          uint4 qa_b[NBQ], qb_b[NBQ];
-#pragma unroll
-          for (int j = 0; j < NBQ; ++j) {
-            qa_b[j] = make_uint4(0, 0, 0, 0);
-            qb_b[j] = qa_b[j];
-            if (ib + j < i1) {
-              const int64_t woff = ((int64_t)(ib + j) * 16 + c * 4) * 4;   // bytes
-              qa_b[j] = ld_stream(rowA + woff);
-              qb_b[j] = ld_stream(rowB + woff);
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < NBQ; ++j) {
-          const int it = ib + j;
-          if (it >= i1) break;
-          const uint4 qa = qa_b[j], qb = qb_b[j];
-          float sa = 1.f, sb = 1.f;
-          uint32_t sa2 = 0, sb2 = 0;
-          if (grp_scale || MODE == kModeInt4Dequant) {
-            const int gi = grp_scale ? (it * 128) / a.group : 0;
-            const uint16_t ua = reinterpret_cast<const uint16_t*>(scA)[gi];
-            const uint16_t ub = reinterpret_cast<const uint16_t*>(scB)[gi];
-            sa = Elem<T>::bits_to_f(ua);
-            sb = Elem<T>::bits_to_f(ub);
-            sa2 = uint32_t(ua) | (uint32_t(ua) << 16);
-            sb2 = uint32_t(ub) | (uint32_t(ub) << 16);
-          }
-          float part[NTB][4];
-#pragma unroll
-          for (int b = 0; b < NTB; ++b)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) part[b][q] = 0.f;
-          const uint32_t qaw[4] = {qa.x, qa.y, qa.z, qa.w};
-          const uint32_t qbw[4] = {qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            uint32_t pa[4], pb[4];
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-              pa[s] = nib_pair<T>(qaw[m], s);
-              pb[s] = nib_pair<T>(qbw[m], s);
-              if (MODE == kModeInt4Dequant) {
-                pa[s] = Mma<T>::mul2(pa[s], sa2);
-                pb[s] = Mma<T>::mul2(pb[s], sb2);
-              }
-            }
-            const int64_t xoff = ((int64_t)it * 128 + c * 32 + m * 8) * (int64_t)sizeof(T);
-#pragma unroll
-            for (int b = 0; b < NTB; ++b) {
-              uint4 xv = make_uint4(0, 0, 0, 0);
-              if (xrow[b]) xv = ld_cached(xrow[b] + xoff);
-              // (x0,x4) (x1,x5) (x2,x6) (x3,x7) to match nibble pairs (s, s+4)
-              const uint32_t x04 = __byte_perm(xv.x, xv.z, 0x5410);
-              const uint32_t x15 = __byte_perm(xv.x, xv.z, 0x7632);
-              const uint32_t x26 = __byte_perm(xv.y, xv.w, 0x5410);
-              const uint32_t x37 = __byte_perm(xv.y, xv.w, 0x7632);
-              if (MODE == kModeInt4Fused && grp_scale) {
-                Mma<T>::run(part[b], pa[0], pb[0], pa[1], pb[1], x04, x15);
-                Mma<T>::run(part[b], pa[2], pb[2], pa[3], pb[3], x26, x37);
-              } else {
-                Mma<T>::run(acc[b], pa[0], pb[0], pa[1], pb[1], x04, x15);
-                Mma<T>::run(acc[b], pa[2], pb[2], pa[3], pb[3], x26, x37);
-              }
-            }
-          }
-          if (MODE == kModeInt4Fused && grp_scale) {
-#pragma unroll
-            for (int b = 0; b < NTB; ++b) {
-              acc[b][0] = fmaf(part[b][0], sa, acc[b][0]);
-              acc[b][1] = fmaf(part[b][1], sa, acc[b][1]);
-              acc[b][2] = fmaf(part[b][2], sb, acc[b][2]);
-              acc[b][3] = fmaf(part[b][3], sb, acc[b][3]);
-            }
-          }
-          }
-        }
+        gemv_kloop<T, MODE, NTB>(rowA, rowB, scA, scB, a.group, i0, i1, xrow, acc);
       }
 
       // -------- cross-warp K reduction (fixed order) ---------------------------

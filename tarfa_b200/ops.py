@@ -307,6 +307,12 @@ def set_gemm_min_tokens(tokens: int) -> None:
     api.check(api.lib().tarfa_b200_set_gemm_min_tokens(int(tokens)))
 
 
+def set_fused_decode_max_tokens(tokens: int) -> None:
+    """``moe_layer`` runs batches of 1..``tokens`` (<= 16) as one persistent
+    kernel; 0 selects the multi-kernel sequence (process-wide, default 16)."""
+    api.check(api.lib().tarfa_b200_set_fused_decode_max_tokens(int(tokens)))
+
+
 def set_stage_events(events) -> None:
     """Record ``events[i]`` (``torch.cuda.Event``) at layer stage boundary ``i``
     (0 start, 1 router/permute, 2 gate_up, 3 down, 4 combine) on this thread;
