@@ -5,7 +5,9 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
 #include <string>
+#include <utility>
 
 #include "../../include/tarfa_b200.h"
 #include <atomic>
@@ -238,7 +240,8 @@ std::atomic<int64_t> g_fused_max_tokens{fused::kMaxT};
 
 bool use_fused_decode(const tarfa_moe_shape& s, const tarfa_moe_weights& w) {
   return s.tokens >= 1 && s.tokens <= g_fused_max_tokens.load() && s.tokens <= fused::kMaxT &&
-         s.top_k <= fused::kMaxK && !use_gemm(s, w, s.shared_inter) && s.hidden % 16 == 0;
+         s.top_k <= fused::kMaxK && !use_gemm(s, w, s.shared_inter) && s.hidden % 16 == 0 &&
+         s.hidden <= 4096;
 }
 
 template <typename T>
@@ -289,13 +292,26 @@ int launch_fused(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
            : mode == kModeInt4Fused ? fused::decode_layer_kernel<T, kModeInt4Fused, 2>
                                     : fused::decode_layer_kernel<T, kModeInt4Dequant, 2>;
   }
+  static std::mutex attr_mu;
+  static std::set<std::pair<int, const void*>> attr_done;
+  {
+    int dev = 0;
+    TARFA_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(attr_mu);
+    if (!attr_done.count({dev, (const void*)kern})) {
+      TARFA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)fused::kSmemBytes));
+      attr_done.insert({dev, (const void*)kern});
+    }
+  }
   int per_sm = 0;
-  TARFA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, fused::kThreads, 0));
+  TARFA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, fused::kThreads,
+                                                           fused::kSmemBytes));
   if (per_sm < 1) return fail(TARFA_ERR_UNSUPPORTED, "fused decode kernel does not fit an SM");
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(sms);          // one CTA per SM, all co-resident (cooperative)
   cfg.blockDim = dim3(fused::kThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = fused::kSmemBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;

@@ -79,8 +79,7 @@ TARFA_DEVI void group_barrier(int id, int nthreads) {
 // One warp's share of a 16-row tile: acc[b] += W(rows g, g+8)[k in iterations
 // [i0, i1)] . x(token block b).  An iteration is 32 k (dense) or 128 k (int4,
 // one scale group).  xrow[b] is this lane's token row (null: zero column).
-// Dense weights are double-buffered in registers: the next 4 iterations'
-// loads are in flight while the current ones feed the tensor cores.
+// Dense weights are loaded 4 iterations (8 x 16 B per lane) at a time.
 template <typename T, int MODE, int NTB>
 TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, const T* scB,
                            int group, int i0, int i1, const char* const (&xrow)[NTB],
@@ -88,46 +87,36 @@ TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, con
   const int c = (threadIdx.x & 31) & 3;
   if (MODE == kModeExact) {
     constexpr int NB = 4;
-    uint4 wa[NB], wb[NB];
+    int it = i0;
+    for (; it + NB <= i1; it += NB) {
+      uint4 wa[NB], wb[NB];
 #pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      wa[j] = make_uint4(0, 0, 0, 0);
-      wb[j] = wa[j];
-      if (i0 + j < i1) {
-        const int64_t off = ((int64_t)(i0 + j) * 32 + c * 8) * (int64_t)sizeof(T);
+      for (int j = 0; j < NB; ++j) {
+        const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
         wa[j] = ld_stream(rowA + off);
         wb[j] = ld_stream(rowB + off);
       }
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
+#pragma unroll
+        for (int b = 0; b < NTB; ++b) {
+          uint4 xv = make_uint4(0, 0, 0, 0);
+          if (xrow[b]) xv = ld_cached(xrow[b] + off);
+          Mma<T>::run(acc[b], wa[j].x, wb[j].x, wa[j].y, wb[j].y, xv.x, xv.y);
+          Mma<T>::run(acc[b], wa[j].z, wb[j].z, wa[j].w, wb[j].w, xv.z, xv.w);
+        }
+      }
     }
-    for (int it = i0; it < i1; it += NB) {
-      uint4 na[NB], nb[NB];
+    for (; it < i1; ++it) {
+      const int64_t off = ((int64_t)it * 32 + c * 8) * (int64_t)sizeof(T);
+      const uint4 wa = ld_stream(rowA + off), wb = ld_stream(rowB + off);
 #pragma unroll
-      for (int j = 0; j < NB; ++j) {
-        na[j] = make_uint4(0, 0, 0, 0);
-        nb[j] = na[j];
-        if (it + NB + j < i1) {
-          const int64_t off = ((int64_t)(it + NB + j) * 32 + c * 8) * (int64_t)sizeof(T);
-          na[j] = ld_stream(rowA + off);
-          nb[j] = ld_stream(rowB + off);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < NB; ++j) {
-        if (it + j < i1) {
-          const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
-#pragma unroll
-          for (int b = 0; b < NTB; ++b) {
-            uint4 xv = make_uint4(0, 0, 0, 0);
-            if (xrow[b]) xv = ld_cached(xrow[b] + off);
-            Mma<T>::run(acc[b], wa[j].x, wb[j].x, wa[j].y, wb[j].y, xv.x, xv.y);
-            Mma<T>::run(acc[b], wa[j].z, wb[j].z, wa[j].w, wb[j].w, xv.z, xv.w);
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < NB; ++j) {
-        wa[j] = na[j];
-        wb[j] = nb[j];
+      for (int b = 0; b < NTB; ++b) {
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (xrow[b]) xv = ld_cached(xrow[b] + off);
+        Mma<T>::run(acc[b], wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
+        Mma<T>::run(acc[b], wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
       }
     }
   } else {
