@@ -236,7 +236,8 @@ bool use_gemm(const tarfa_moe_shape& s, const tarfa_moe_weights& w, int64_t Is) 
 }
 
 // Largest batch that takes the fused single-launch decode kernel (0: never).
-std::atomic<int64_t> g_fused_max_tokens{fused::kMaxT};
+// Off by default: measured slower than the multi-kernel sequence so far.
+std::atomic<int64_t> g_fused_max_tokens{0};
 
 bool use_fused_decode(const tarfa_moe_shape& s, const tarfa_moe_weights& w) {
   return s.tokens >= 1 && s.tokens <= g_fused_max_tokens.load() && s.tokens <= fused::kMaxT &&

@@ -309,7 +309,7 @@ def set_gemm_min_tokens(tokens: int) -> None:
 
 def set_fused_decode_max_tokens(tokens: int) -> None:
     """``moe_layer`` runs batches of 1..``tokens`` (<= 16) as one persistent
-    kernel; 0 selects the multi-kernel sequence (process-wide, default 16)."""
+    kernel; 0 selects the multi-kernel sequence (process-wide, default 0)."""
     api.check(api.lib().tarfa_b200_set_fused_decode_max_tokens(int(tokens)))
 
 

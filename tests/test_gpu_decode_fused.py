@@ -23,8 +23,9 @@ def _cuda():
     from tarfa_b200 import build
     build.build()
     ops.device_status(clear=True)
+    ops.set_fused_decode_max_tokens(16)       # this module exercises the fused kernel
     yield
-    ops.set_fused_decode_max_tokens(16)
+    ops.set_fused_decode_max_tokens(0)
     torch.cuda.synchronize()
     assert ops.device_status() == 0, "a kernel raised a device status bit (timeout / bad id)"
 
