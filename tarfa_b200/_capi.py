@@ -17,7 +17,7 @@ ABI_VERSION = 1
 TARFA_OK, TARFA_ERR_INVALID, TARFA_ERR_UNSUPPORTED, TARFA_ERR_WORKSPACE, TARFA_ERR_CUDA = range(5)
 TARFA_BF16, TARFA_F16 = 0, 1
 TARFA_W_DENSE, TARFA_W_INT4 = 0, 1
-OP_EXPERTS, OP_MOE_LAYER, OP_ROUTER, OP_PERMUTE = 0, 1, 2, 3
+OP_EXPERTS, OP_MOE_LAYER, OP_ROUTER, OP_PERMUTE, OP_SHARED = 0, 1, 2, 3, 4
 DEV_BAD_EXPERT_ID, DEV_WAIT_TIMEOUT = 1, 2
 
 
@@ -60,6 +60,9 @@ SIGNATURES = {
     "tarfa_b200_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int32, _P]),
     "tarfa_b200_set_stage_events": (C.c_int, [C.POINTER(C.c_void_p), C.c_int32]),
     "tarfa_b200_set_gemm_min_tokens": (C.c_int, [C.c_int64]),
+    "tarfa_b200_shared_expert": (C.c_int, [C.POINTER(MoeShape), _P, C.POINTER(SharedExpert), _P, _P,
+                                           C.c_size_t, _P]),
+    "tarfa_b200_combine_routes": (C.c_int, [C.POINTER(MoeShape), _P, _P, _P, _P, _P, _P]),
     "tarfa_b200_set_fused_decode_max_tokens": (C.c_int, [C.c_int64]),
 }
 

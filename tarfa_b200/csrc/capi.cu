@@ -140,6 +140,16 @@ Ws layout(const tarfa_moe_shape& s, int op) {
   w.bar = 16;
   w.hb_cnt = 32;   // 8192 / 16 counters at most (hidden <= 8192)
   o = kZeroHeaderBytes;
+  if (op == TARFA_OP_SHARED) {   // shared expert alone: one unit of T rows
+    const int64_t Iss = s.shared_inter;
+    w.units = take(8 * 4);
+    w.perm_tok = take((T > 0 ? T : 1) * 4);
+    w.gate_logit = take(T * 4);
+    w.act = take(T * Iss * 2);
+    w.y = take(T * H * 4);
+    w.total = o;
+    return w;
+  }
   w.units = take((4 + 4 * Umax) * 4);
   w.idx32 = take(R * 4);
   w.topw = take(R * 4);
@@ -735,6 +745,88 @@ int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
     if (!rc) rc = run_combine<__half>(s, L, workspace, at<float>(workspace, L.topw), int4, sh != nullptr, use_gemm(s, *weights, s.shared_inter), out, st);
   }
   return rc;
+}
+
+int tarfa_b200_shared_expert(const tarfa_moe_shape* shape, const void* hidden,
+                             const tarfa_shared_expert* shared, void* out, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (int rc = check_shape(shape)) return rc;
+  if (shape->tokens == 0) return TARFA_OK;
+  TARFA_CHECK(shape->shared_inter > 0, "shared_inter must be > 0");
+  TARFA_CHECK(hidden && out && shared && shared->gate_proj && shared->up_proj &&
+                  shared->down_proj && shared->gate_weight,
+              "null argument");
+  TARFA_CHECK(aligned16(hidden) && aligned16(shared->gate_proj) && aligned16(shared->up_proj) &&
+                  aligned16(shared->down_proj) && aligned16(shared->gate_weight),
+              "operands not 16-byte aligned");
+  const Ws L = layout(*shape, TARFA_OP_SHARED);
+  if (workspace_bytes < L.total || !workspace)
+    return fail(TARFA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, L.total);
+  unsigned* status;
+  int sms;
+  if (int rc = device_info(&status, &sms)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int T_ = (int)shape->tokens, H = (int)shape->hidden, Is = (int)shape->shared_inter;
+  GemvArgs g{};
+  g.units = at<int32_t>(workspace, L.units);
+  g.which = 2;
+  g.E = (int)shape->experts;
+  g.status = status;
+  g.x = hidden;
+  g.ld_x = H;
+  g.perm_tok = at<int32_t>(workspace, L.perm_tok);
+  g.N_s = Is;
+  g.K_s = H;
+  g.sw0 = shared->gate_proj;
+  g.sw1 = shared->up_proj;
+  g.out = at<void>(workspace, L.act);
+  g.ld_out = Is;
+  auto run = [&](auto tag) -> int {
+    using T = decltype(tag);
+    shared_prep_kernel<T><<<(T_ + 7) / 8, 256, 0, st>>>(
+        static_cast<const T*>(hidden), static_cast<const T*>(shared->gate_weight), T_, H,
+        at<int32_t>(workspace, L.units), at<int32_t>(workspace, L.perm_tok),
+        at<float>(workspace, L.gate_logit));
+    TARFA_CUDA(cudaGetLastError());
+    if (int rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(g, Is / 8, T_, sms, st)) return rc;
+    GemvArgs d = g;
+    d.x = at<void>(workspace, L.act);
+    d.ld_x = Is;
+    d.perm_tok = nullptr;
+    d.N_s = H;
+    d.K_s = Is;
+    d.sw0 = shared->down_proj;
+    d.sw1 = nullptr;
+    d.out = at<void>(workspace, L.y);
+    d.ld_out = H;
+    if (int rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(d, H / 16, T_, sms, st)) return rc;
+    shared_finish_kernel<T><<<dim3((H + 255) / 256, T_), 256, 0, st>>>(
+        at<float>(workspace, L.y), at<float>(workspace, L.gate_logit), T_, H, static_cast<T*>(out));
+    TARFA_CUDA(cudaGetLastError());
+    return TARFA_OK;
+  };
+  return shape->dtype == TARFA_BF16 ? run(__nv_bfloat16{}) : run(__half{});
+}
+
+int tarfa_b200_combine_routes(const tarfa_moe_shape* shape, const void* y_routes,
+                              const int64_t* top_idx, const float* top_w,
+                              const void* shared_gated, void* out, void* stream) {
+  if (int rc = check_shape(shape)) return rc;
+  if (shape->tokens == 0) return TARFA_OK;
+  TARFA_CHECK(y_routes && top_idx && top_w && out, "null argument");
+  const int T_ = (int)shape->tokens, K = shape->top_k, H = (int)shape->hidden, E = (int)shape->experts;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((H + 255) / 256, T_);
+  if (shape->dtype == TARFA_BF16)
+    combine_routes_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(y_routes), top_idx, top_w,
+        static_cast<const __nv_bfloat16*>(shared_gated), T_, K, H, E, static_cast<__nv_bfloat16*>(out));
+  else
+    combine_routes_kernel<__half><<<grid, 256, 0, st>>>(
+        static_cast<const __half*>(y_routes), top_idx, top_w, static_cast<const __half*>(shared_gated),
+        T_, K, H, E, static_cast<__half*>(out));
+  TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
 }
 
 // The whole layer with the library's own static scratch instead of a

@@ -224,6 +224,40 @@ def moe_layer(h: torch.Tensor, w_r: torch.Tensor, weights: ExpertWeights,
     return (out, idx, wt) if return_routing else out
 
 
+def shared_expert(h: torch.Tensor, shared: SharedWeights, out: torch.Tensor | None = None):
+    """``sigmoid(shared_expert_gate(h)) * shared_expert(h)`` alone, ``[T, H]``."""
+    _need_cuda(h, out)
+    T, H = h.shape
+    Is = shared.gate_proj.shape[0]
+    if out is None:
+        out = torch.empty_like(h)
+    shape = _shape(T, H, 1, 32, Is, 1, h.dtype)
+    L = api.lib()
+    ws = workspace(L.tarfa_b200_workspace_size(C.byref(shape), api.OP_SHARED), h.device)
+    sc = shared.c_struct()
+    api.check(L.tarfa_b200_shared_expert(C.byref(shape), _ptr(h), C.byref(sc), _ptr(out), _ptr(ws),
+                                         ws.numel(), _stream(h.device)))
+    return out
+
+
+def combine_routes(y_routes: torch.Tensor, top_idx: torch.Tensor, top_w: torch.Tensor,
+                   num_experts: int, shared_gated: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Reference-order combine of per-route expert outputs ``y_routes [T*K, H]``."""
+    _need_cuda(y_routes, top_idx, top_w, shared_gated, out)
+    T, K = top_idx.shape
+    H = y_routes.shape[1]
+    if y_routes.shape[0] != T * K or top_idx.dtype != torch.int64 or top_w.dtype != torch.float32:
+        raise RuntimeError("y_routes [T*K, H], top_idx int64 [T, K], top_w fp32 [T, K]")
+    if out is None:
+        out = torch.empty((T, H), dtype=y_routes.dtype, device=y_routes.device)
+    shape = _shape(T, H, num_experts, 32, 0, K, y_routes.dtype)
+    api.check(api.lib().tarfa_b200_combine_routes(C.byref(shape), _ptr(y_routes), _ptr(top_idx),
+                                                  _ptr(top_w), _ptr(shared_gated), _ptr(out),
+                                                  _stream(y_routes.device)))
+    return out
+
+
 class MoePlan:
     """A prepared ``moe_layer`` call on fixed device buffers.
 
