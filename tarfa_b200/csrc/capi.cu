@@ -235,6 +235,7 @@ int launch_gemv_ntb(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStrea
 
 constexpr int kKsplitGateUp = 8;
 constexpr int kKsplitDown = 4;
+constexpr int64_t kRouterGemmMinTokens = 128;   // from here the router logits use the tensor cores
 
 // Token count from which dense layers take the tcgen05 grouped-GEMM path
 // (tarfa_b200_set_gemm_min_tokens); below it the tensor-core GEMV path.
@@ -487,9 +488,9 @@ int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* to
   c.mode = !int4 ? kModeExact : (T_ == 1 ? kModeInt4Fused : kModeInt4Dequant);
   c.gate_logit = with_shared ? at<float>(ws, L.gate_logit) : nullptr;
   c.out = out;
-  dim3 grid((H + 255) / 256, T_);
-  if (gemm_y) combine_kernel<T, T><<<grid, 256, 0, st>>>(c);   // GEMM path: y in the model dtype
-  else combine_kernel<T, float><<<grid, 256, 0, st>>>(c);
+  (void)H;
+  if (gemm_y) combine_token_kernel<T, T><<<T_, 256, 0, st>>>(c);   // GEMM path: y in the model dtype
+  else combine_token_kernel<T, float><<<T_, 256, 0, st>>>(c);
   TARFA_CUDA(cudaGetLastError());
   stage_mark(4, st);
   return TARFA_OK;
@@ -520,6 +521,29 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
                   const void* w_sg, const Ws& L, void* ws, int64_t* idx_out, float* w_out,
                   float* logits_out, bool permute, bool add_shared, unsigned* status,
                   cudaStream_t st) {
+  if (s.tokens >= kRouterGemmMinTokens && s.experts >= 128 &&
+      router_gemm_supported(s.hidden, s.experts)) {
+    // large batch: fp32 logits on the tensor cores, exact-rounding fixup + top-k, permute
+    unsigned* st_ptr;
+    int sms;
+    if (int rc = device_info(&st_ptr, &sms)) return rc;
+    const int T_ = (int)s.tokens, H = (int)s.hidden, E = (int)s.experts, K = s.top_k;
+    const char* err = nullptr;
+    if (router_logits_sm100(s.dtype == TARFA_BF16, hidden, T_, H, w_r, E, at<int32_t>(ws, L.units),
+                            at<float>(ws, L.logits), status, sms, st, &err))
+      return fail(TARFA_ERR_CUDA, "%s", err ? err : "router logits");
+    const int grid = (T_ + 7) / 8;
+    topk_fixup_kernel<T><<<grid, 256, 0, st>>>(
+        at<float>(ws, L.logits), static_cast<const T*>(hidden), static_cast<const T*>(w_r),
+        static_cast<const T*>(bias), static_cast<const T*>(w_sg), T_, H, E, K, at<float>(ws, L.logits),
+        at<float>(ws, L.gate_logit), at<int32_t>(ws, L.idx32), at<float>(ws, L.topw), idx_out, w_out,
+        logits_out);
+    TARFA_CUDA(cudaGetLastError());
+    if (!permute) return TARFA_OK;
+    PermuteOut o{nullptr, at<int32_t>(ws, L.perm_tok), at<int32_t>(ws, L.perm_slot),
+                 at<int32_t>(ws, L.route_row), at<int32_t>(ws, L.units), nullptr};
+    return launch_permute<int32_t>(at<int32_t>(ws, L.idx32), T_, K, E, add_shared, o, status, st);
+  }
   RouterArgs a{};
   a.h = hidden;
   a.w_r = w_r;

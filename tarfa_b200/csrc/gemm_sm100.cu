@@ -140,6 +140,40 @@ int run(const PrefillArgs& a, cudaStream_t st, const char** err) {
 
 }  // namespace
 
+bool router_gemm_supported(int64_t H, int64_t E) { return H % 64 == 0 && E % 16 == 0 && E <= 1024; }
+
+int router_logits_sm100(bool bf16, const void* h, int64_t T, int64_t H, const void* w_r, int64_t E,
+                        int32_t* units, float* logits, unsigned* status, int sms, cudaStream_t st,
+                        const char** err) {
+  if (!encoder()) {
+    *err = "cuTensorMapEncodeTiled is not available from the driver";
+    return 1;
+  }
+  sm100::single_unit_kernel<<<1, 32, 0, st>>>(units, (int)E, (int)T);
+  if (cudaGetLastError() != cudaSuccess) { *err = "unit table launch failed"; return 1; }
+  CUtensorMap mA, mW;
+  if (!make_map(&mA, h, (uint64_t)T, (uint64_t)H, 128, bf16) ||
+      !make_map(&mW, w_r, (uint64_t)E, (uint64_t)H, 128, bf16)) {
+    *err = "cuTensorMapEncodeTiled failed (router)";
+    return 1;
+  }
+  sm100::Params p{};
+  p.E = (int)E;
+  p.K_r = (int)H;
+  p.K_s = (int)H;
+  p.N_r = (int)E;
+  p.N_s = (int)E;
+  p.units = units;
+  p.out = logits;
+  p.ldo = E;
+  p.status = status;
+  p.idesc = sm100::make_idesc(bf16);
+  const int64_t tiles = ((T + sm100::BM - 1) / sm100::BM) * ((E + sm100::BN - 1) / sm100::BN);
+  const int grid = (int)std::min<int64_t>(sms, tiles);
+  return bf16 ? launch_phase<__nv_bfloat16, 2>(mA, mW, mW, mW, p, grid, st, err)
+              : launch_phase<__half, 2>(mA, mW, mW, mW, p, grid, st, err);
+}
+
 bool prefill_supported(int64_t H, int64_t I, int64_t Is, bool dense) {
   return dense && H % 256 == 0 && I % 128 == 0 && Is % 128 == 0 && H <= 65536 && I <= 65536;
 }

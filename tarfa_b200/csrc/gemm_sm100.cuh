@@ -187,7 +187,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   const int ntot = nu + p.units[2];
   const UnitDesc* descs = unit_descs(p.units);
   const int nt_r = PHASE == 0 ? p.N_r / 128 : p.N_r / BN;   // n-tiles per routed unit
-  const int nt_s = PHASE == 0 ? p.N_s / 128 : p.N_s / BN;   // n-tiles of the shared unit
+  const int nt_s = PHASE == 0 ? p.N_s / 128 : (p.N_s + BN - 1) / BN;   // n-tiles of the shared unit
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -364,6 +364,27 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
           }
         }
+      } else if (PHASE == 2) {
+        // plain fp32 store (router logits), columns masked at N_s
+#pragma unroll 1
+        for (int j0 = 0; j0 < BN; j0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tb + j0, v);
+          tmem_wait_ld();
+          const int col0 = ti.n * BN + j0;
+          if (valid && col0 < p.N_s) {
+            float* dst = static_cast<float*>(p.out) + orow * p.ldo + col0;
+            if (col0 + 16 <= p.N_s) {
+              float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                d4[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                    __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            } else {
+              for (int j = 0; j < 16 && col0 + j < p.N_s; ++j) dst[j] = __uint_as_float(v[j]);
+            }
+          }
+        }
       } else {
 #pragma unroll 1
         for (int j0 = 0; j0 < BN; j0 += 16) {
@@ -394,6 +415,18 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   if (warp == 2) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// A unit table with one unit covering rows [0, T) (marked as the "shared" unit,
+// expert id E), used to run a plain [T, K] x [N, K]^T product through the kernel.
+__global__ void single_unit_kernel(int32_t* units, int E, int T) {
+  if (threadIdx.x == 0) {
+    units[0] = 0;
+    units[1] = 0;
+    units[2] = 1;
+    units[3] = 0;
+    reinterpret_cast<UnitDesc*>(units + 4)[0] = UnitDesc{E, 0, T, 0};
   }
 }
 
