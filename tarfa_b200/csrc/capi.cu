@@ -488,9 +488,14 @@ int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* to
   c.mode = !int4 ? kModeExact : (T_ == 1 ? kModeInt4Fused : kModeInt4Dequant);
   c.gate_logit = with_shared ? at<float>(ws, L.gate_logit) : nullptr;
   c.out = out;
-  (void)H;
-  if (gemm_y) combine_token_kernel<T, T><<<T_, 256, 0, st>>>(c);   // GEMM path: y in the model dtype
-  else combine_token_kernel<T, float><<<T_, 256, 0, st>>>(c);
+  if (T_ > 64) {   // large batch: one block per token, slot order sorted once
+    if (gemm_y) combine_token_kernel<T, T><<<T_, 256, 0, st>>>(c);   // GEMM path: y in model dtype
+    else combine_token_kernel<T, float><<<T_, 256, 0, st>>>(c);
+  } else {         // decode: thread per (token, column), many small blocks
+    const dim3 grid((H + 127) / 128, T_);
+    if (gemm_y) combine_kernel<T, T><<<grid, 128, 0, st>>>(c);
+    else combine_kernel<T, float><<<grid, 128, 0, st>>>(c);
+  }
   TARFA_CUDA(cudaGetLastError());
   stage_mark(4, st);
   return TARFA_OK;
