@@ -1,0 +1,87 @@
+"""Synthetic MoE-only decoder stack for whole-model measurements.
+
+``n_layers`` x (``h = h + MoE(RMSNorm(h))``) between an embedding and an fp32
+LM head with greedy argmax: the MoE path of the reference's decoder layer
+(``modeling_qwen3_5_moe.py:828-870``: post-attention RMSNorm, sparse MoE block,
+residual) with attention left out, and the reference's fp32 final logits
+(``serve.py:128-132``).  Weights are synthetic, regenerable per (layer, expert)
+(``tarfa_b200.synthetic``); the routed experts come from a
+``StreamingExpertTier`` (resident + pinned-host streaming) or are all resident.
+
+RMSNorm follows ``Qwen3_5MoeRMSNorm`` (modeling_qwen3_5_moe.py:795-808):
+``(x.float() * rsqrt(mean(x^2) + eps) * (1 + w)).to(x.dtype)``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+from . import synthetic as syn
+from .streaming import StreamingExpertTier
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + w.float())).to(x.dtype)
+
+
+class SyntheticStack:
+    def __init__(self, shape: syn.LayerShape, n_layers: int, vocab: int, device, seed: int = 0,
+                 resident: int | None = None, staging: int = 64, dtype=torch.bfloat16):
+        self.s, self.n, self.V = shape, n_layers, vocab
+        self.device = torch.device(device)
+        self.dtype = dtype
+        g = torch.Generator(device=self.device).manual_seed(syn._mix(seed, 0xE5))
+
+        def n(shape_, std):
+            t = torch.empty(shape_, dtype=torch.float32, device=self.device)
+            t.normal_(0.0, std, generator=g)
+            return t.to(dtype)
+
+        self.embed = n((vocab, shape.hidden), 1.0)
+        self.lm_head = n((vocab, shape.hidden), 0.02)
+        self.final_norm = n((shape.hidden,), 0.1)
+        R = shape.experts if resident is None else resident
+        self.tier = StreamingExpertTier(n_layers, shape.experts, shape.hidden, shape.inter, R,
+                                        max(1, staging), self.device, dtype)
+        self.layers = []
+        for l in range(n_layers):
+            L = syn.layer_device(syn._mix(seed, l), shape, self.device, dtype)
+            self.tier.load_layer(l, L["gate_up"], L["down"])
+            self.layers.append({
+                "norm": n((shape.hidden,), 0.1), "router": L["router"],
+                "shared": ops.SharedWeights(L["sh_gate"], L["sh_up"], L["sh_down"], L["sh_gate_w"]),
+            })
+            del L
+        self._prev = [None] * n_layers
+
+    def layer_weights_cpu(self, l: int):
+        """(gate_up, down) of all experts of layer l, on the CPU (for the oracle)."""
+        R = self.tier.R
+        gu = torch.empty((self.s.experts, 2 * self.s.inter, self.s.hidden), dtype=self.dtype)
+        dn = torch.empty((self.s.experts, self.s.hidden, self.s.inter), dtype=self.dtype)
+        if R:
+            gu[:R] = self.tier.gate_up[l * R:(l + 1) * R].cpu()
+            dn[:R] = self.tier.down[l * R:(l + 1) * R].cpu()
+        if R < self.s.experts:
+            gu[R:] = self.tier.host_gu[l]
+            dn[R:] = self.tier.host_dn[l]
+        return gu, dn
+
+    @torch.no_grad()
+    def step(self, tokens: torch.Tensor, prefetch: bool = True) -> torch.Tensor:
+        """One decode step for a batch of token ids -> next token ids (greedy)."""
+        h = self.embed.index_select(0, tokens.to(self.device))
+        for l, layer in enumerate(self.layers):
+            x = rms_norm(h, layer["norm"])
+            idx, w = ops.router_topk(x, layer["router"], self.s.top_k)
+            ids = torch.unique(idx).tolist()       # routed ids on the host (fused_int4.py:166)
+            weights = self.tier.weights_for(l, ids)
+            if prefetch and l + 1 < self.n and self._prev[l + 1] is not None:
+                self.tier.prefetch(l + 1, self._prev[l + 1])   # PIPE-style prediction
+            self._prev[l] = ids
+            routed = ops.experts_forward(x, idx, w, weights)
+            h = h + (routed + ops.shared_expert(x, layer["shared"]))
+        hf = rms_norm(h, self.final_norm)
+        logits = hf.float() @ self.lm_head.float().t()          # fp32 logits
+        return logits.argmax(-1)
