@@ -1,6 +1,7 @@
 // C ABI of tarfa_b200: argument checks, workspace layout and launch sequence.
 // Declarations and the reference interface each entry point replaces are in
 // include/tarfa_b200.h.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -116,7 +117,7 @@ int noalloc_scratch(void** out) {
 // ---------------------------------------------------------------------------
 struct Ws {
   size_t counter, logits, gate_logit, idx32, topw, units, perm_tok, perm_slot, route_row, act, y,
-      xperm, bar, hb_cnt;
+      xperm, bar, hb_cnt, wnorm;
   size_t total;
 };
 
@@ -159,6 +160,7 @@ Ws layout(const tarfa_moe_shape& s, int op) {
   if (op == TARFA_OP_MOE_LAYER || op == TARFA_OP_ROUTER) {
     w.logits = take(T * E * 4);
     w.gate_logit = take(T * 4);
+    w.wnorm = take(E * 4);
   }
   if (op == TARFA_OP_MOE_LAYER || op == TARFA_OP_EXPERTS) {
     w.act = take(Rt * Imax * 2);
@@ -215,22 +217,46 @@ int check_weights(const tarfa_moe_shape* s, const tarfa_moe_weights* w) {
 // ---------------------------------------------------------------------------
 // launches
 // ---------------------------------------------------------------------------
+// Launch, optionally as a programmatic dependent of the previous kernel on the
+// stream (it may start before that kernel ends and synchronises with
+// griddepcontrol.wait).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     bool pdl, Args&&... args) {
+  if (!pdl) {
+    kern<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <typename T, int MODE, int PHASE, int KSPLIT, int NTB>
-int launch_gemv(const GemvArgs& a, int max_tiles, int sms, cudaStream_t st) {
+int launch_gemv(const GemvArgs& a, int max_tiles, int sms, cudaStream_t st, bool pdl, int smem) {
   constexpr int groups = kGemvWarps / KSPLIT;
   int grid = (max_tiles + groups - 1) / groups;
   const int cap = 2 * sms;
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
-  gemv_kernel<T, MODE, PHASE, KSPLIT, NTB><<<grid, kGemvThreads, 0, st>>>(a);
-  TARFA_CUDA(cudaGetLastError());
+  TARFA_CUDA(launch_k(gemv_kernel<T, MODE, PHASE, KSPLIT, NTB>, dim3(grid), dim3(kGemvThreads),
+                      (size_t)smem, st, pdl, a));
   return TARFA_OK;
 }
 
 template <typename T, int MODE, int PHASE, int KSPLIT>
-int launch_gemv_ntb(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStream_t st) {
-  if (T_ <= 8) return launch_gemv<T, MODE, PHASE, KSPLIT, 1>(a, max_tiles, sms, st);
-  return launch_gemv<T, MODE, PHASE, KSPLIT, 2>(a, max_tiles, sms, st);
+int launch_gemv_ntb(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStream_t st,
+                    bool pdl = false, int smem = 0) {
+  if (T_ <= 8) return launch_gemv<T, MODE, PHASE, KSPLIT, 1>(a, max_tiles, sms, st, pdl, smem);
+  return launch_gemv<T, MODE, PHASE, KSPLIT, 2>(a, max_tiles, sms, st, pdl, smem);
 }
 
 constexpr int kKsplitGateUp = 8;
@@ -335,9 +361,11 @@ int launch_fused(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
 }
 
 template <typename T>
+// dr: in-kernel routing of a decode batch (the gate_up GEMV routes from the
+// router kernel's logits; every launch is a programmatic dependent).
 int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_weights& w,
                 const tarfa_shared_expert* sh, const Ws& L, void* ws, void* out,
-                unsigned* status, int sms, cudaStream_t st) {
+                unsigned* status, int sms, cudaStream_t st, const DecodeRoute* dr = nullptr) {
   const int T_ = (int)s.tokens, K = s.top_k, E = (int)s.experts, H = (int)s.hidden;
   const int I = (int)s.inter, Is = sh ? (int)s.shared_inter : 0;
   const int Imax = I > Is ? I : Is;
@@ -410,19 +438,29 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
     g.w_rstride = H;
   }
   const int tiles_gu = Umax * (I / 8) + (Is ? Is / 8 : 0);
+  const bool pdl = dr != nullptr;
+  int smem = 0;
+  if (dr) {
+    g.route_mode = 1;
+    g.route = *dr;
+    smem = route_smem_ints(T_, K, E, kGemvWarps) * (int)sizeof(int);
+  }
   int rc;
   if (!int4) {
     g.which = 3;
-    rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st);
+    rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st, pdl, smem);
   } else {
     g.which = 1;
     rc = mode == kModeInt4Fused
-             ? launch_gemv_ntb<T, kModeInt4Fused, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st)
-             : launch_gemv_ntb<T, kModeInt4Dequant, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st);
+             ? launch_gemv_ntb<T, kModeInt4Fused, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st,
+                                                                          pdl, smem)
+             : launch_gemv_ntb<T, kModeInt4Dequant, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms,
+                                                                            st, pdl, smem);
     if (rc == TARFA_OK && Is) {
       GemvArgs gs = g;
       gs.which = 2;
-      rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(gs, Is / 8, T_, sms, st);
+      if (dr) gs.route_mode = 2;   // fixed shared rows; the routed launch routes
+      rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(gs, Is / 8, T_, sms, st, pdl);
     }
   }
   if (rc) return rc;
@@ -440,6 +478,7 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
   g.out = at<void>(ws, L.y);
   g.ld_out = H;
   g.w = w.down;
+  g.route_mode = 0;   // the unit table is in the workspace now
   if (int4) {
     g.w_estride = (int64_t)H * I / 8;
     g.w_rstride = I / 8;
@@ -453,16 +492,17 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
   const int tiles_dn = (Umax + (Is ? 1 : 0)) * (H / 16);
   if (!int4) {
     g.which = 3;
-    rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st);
+    rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st, pdl);
   } else {
     g.which = 1;
     rc = mode == kModeInt4Fused
-             ? launch_gemv_ntb<T, kModeInt4Fused, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st)
-             : launch_gemv_ntb<T, kModeInt4Dequant, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st);
+             ? launch_gemv_ntb<T, kModeInt4Fused, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st, pdl)
+             : launch_gemv_ntb<T, kModeInt4Dequant, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st,
+                                                                        pdl);
     if (rc == TARFA_OK && Is) {
       GemvArgs gs = g;
       gs.which = 2;
-      rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(gs, H / 16, T_, sms, st);
+      rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(gs, H / 16, T_, sms, st, pdl);
     }
   }
   if (rc) return rc;
@@ -472,7 +512,7 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
 
 template <typename T>
 int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* top_w, bool int4,
-                bool with_shared, bool gemm_y, void* out, cudaStream_t st) {
+                bool with_shared, bool gemm_y, void* out, cudaStream_t st, bool pdl = false) {
   const int T_ = (int)s.tokens, K = s.top_k, H = (int)s.hidden;
   CombineArgs c{};
   c.y = at<void>(ws, L.y);
@@ -493,8 +533,8 @@ int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* to
     else combine_token_kernel<T, float><<<T_, 256, 0, st>>>(c);
   } else {         // decode: thread per (token, column), many small blocks
     const dim3 grid((H + 127) / 128, T_);
-    if (gemm_y) combine_kernel<T, T><<<grid, 128, 0, st>>>(c);
-    else combine_kernel<T, float><<<grid, 128, 0, st>>>(c);
+    if (gemm_y) TARFA_CUDA(launch_k(combine_kernel<T, T>, grid, dim3(128), 0, st, pdl, c));
+    else TARFA_CUDA(launch_k(combine_kernel<T, float>, grid, dim3(128), 0, st, pdl, c));
   }
   TARFA_CUDA(cudaGetLastError());
   stage_mark(4, st);
@@ -537,10 +577,13 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
     if (router_logits_sm100(s.dtype == TARFA_BF16, hidden, T_, H, w_r, E, at<int32_t>(ws, L.units),
                             at<float>(ws, L.logits), status, sms, st, &err))
       return fail(TARFA_ERR_CUDA, "%s", err ? err : "router logits");
+    row_norms_kernel<T><<<(E + 7) / 8, 256, 0, st>>>(static_cast<const T*>(w_r), E, H,
+                                                     at<float>(ws, L.wnorm));
     const int grid = (T_ + 7) / 8;
     topk_fixup_kernel<T><<<grid, 256, 0, st>>>(
         at<float>(ws, L.logits), static_cast<const T*>(hidden), static_cast<const T*>(w_r),
-        static_cast<const T*>(bias), static_cast<const T*>(w_sg), T_, H, E, K, at<float>(ws, L.logits),
+        static_cast<const T*>(bias), static_cast<const T*>(w_sg), at<float>(ws, L.wnorm), T_, H, E,
+        K, at<float>(ws, L.logits),
         at<float>(ws, L.gate_logit), at<int32_t>(ws, L.idx32), at<float>(ws, L.topw), idx_out, w_out,
         logits_out);
     TARFA_CUDA(cudaGetLastError());
@@ -573,8 +616,16 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
   a.status = status;
   const int rows = a.E + (w_sg ? 1 : 0);
   const int warps = kRouterThreads / 32;
-  const int grid = (rows + warps - 1) / warps;
-  const int smem = permute ? permute_smem_bytes(warps, a.E) : 0;
+  unsigned* st_unused;
+  int sms;
+  if (int rc = device_info(&st_unused, &sms)) return rc;
+  // work items = rows x token groups; about two warps' worth per warp slot of one wave
+  const int64_t target = 2LL * sms * warps;
+  a.tpw = (int)std::max<int64_t>(1, std::min<int64_t>(a.T, ((int64_t)rows * a.T + target - 1) / target));
+  const int64_t items = (int64_t)rows * ((a.T + a.tpw - 1) / a.tpw);
+  const int grid = (int)((items + warps - 1) / warps);
+  const int smem = permute_smem_bytes(warps, a.E) +
+                   (a.T * a.K <= kRouterSmemIdx ? a.T * a.K * (int)sizeof(int32_t) : 0);
   const int per_lane = (a.H / 8 + 31) / 32;
 #define TARFA_ROUTER(MC)                                                                  \
   router_kernel<T, MC><<<grid, kRouterThreads, smem, st>>>(a)
@@ -593,6 +644,81 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
 // ===========================================================================
 // exported entry points
 // ===========================================================================
+// Decode batches on the GEMV path route inside the gate_up kernel (routing.cuh):
+// the router kernel only writes logits, and the expert kernels are programmatic
+// dependents of one another.
+bool use_decode_routing(const tarfa_moe_shape& s, const tarfa_moe_weights& w) {
+  return s.tokens <= 16 && s.tokens * s.top_k <= 128 && s.experts <= 1024 &&
+         !use_gemm(s, w, s.shared_inter) && !use_fused_decode(s, w);
+}
+
+template <typename T>
+int launch_router_logits(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
+                         const void* bias, const void* w_sg, const Ws& L, void* ws, int sms,
+                         cudaStream_t st) {
+  RouterArgs a{};
+  a.h = hidden;
+  a.w_r = w_r;
+  a.bias = bias;
+  a.w_sg = w_sg;
+  a.T = (int)s.tokens;
+  a.H = (int)s.hidden;
+  a.E = (int)s.experts;
+  a.K = s.top_k;
+  a.logits = at<float>(ws, L.logits);
+  a.gate_logit = at<float>(ws, L.gate_logit);
+  const int rows = a.E + (w_sg ? 1 : 0);
+  constexpr int warps = kRouterThreads / 32;
+  if (a.T <= 2) {            // latency: split each row over four warps
+    a.wpr = 4;
+    a.tpw = 1;
+  } else {                   // throughput: a row per warp, tokens grouped
+    a.wpr = 1;
+    const int64_t target = 2LL * sms * warps;
+    a.tpw = (int)std::max<int64_t>(1, std::min<int64_t>(a.T, ((int64_t)rows * a.T + target - 1) / target));
+  }
+  const int slots = warps / a.wpr;
+  const int64_t items = (int64_t)rows * ((a.T + a.tpw - 1) / a.tpw);
+  const int grid = (int)((items + slots - 1) / slots);
+  const int per_lane = ((a.H / 8 + a.wpr - 1) / a.wpr + 31) / 32;
+#define TARFA_ROUTER_LOGITS(MC) router_logits_kernel<T, MC><<<grid, kRouterThreads, 0, st>>>(a)
+  if (per_lane <= 2) TARFA_ROUTER_LOGITS(2);
+  else if (per_lane <= 4) TARFA_ROUTER_LOGITS(4);
+  else if (per_lane <= 8) TARFA_ROUTER_LOGITS(8);
+  else if (per_lane <= 16) TARFA_ROUTER_LOGITS(16);
+  else TARFA_ROUTER_LOGITS(32);
+#undef TARFA_ROUTER_LOGITS
+  TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
+}
+
+template <typename T>
+int run_decode_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
+                     const void* bias, const tarfa_moe_weights& w, const tarfa_shared_expert* sh,
+                     void* out, int64_t* idx_out, float* w_out, const Ws& L, void* ws,
+                     unsigned* status, int sms, cudaStream_t st) {
+  if (int rc = launch_router_logits<T>(s, hidden, w_r, bias, sh ? sh->gate_weight : nullptr, L, ws,
+                                       sms, st))
+    return rc;
+  stage_mark(1, st);
+  DecodeRoute dr{};
+  dr.logits = at<float>(ws, L.logits);
+  dr.T = (int)s.tokens;
+  dr.K = s.top_k;
+  dr.add_shared = sh != nullptr;
+  dr.g_units = at<int32_t>(ws, L.units);
+  dr.g_perm_tok = at<int32_t>(ws, L.perm_tok);
+  dr.g_perm_slot = at<int32_t>(ws, L.perm_slot);
+  dr.g_route_row = at<int32_t>(ws, L.route_row);
+  dr.g_idx32 = at<int32_t>(ws, L.idx32);
+  dr.g_topw = at<float>(ws, L.topw);
+  dr.idx_out = idx_out;
+  dr.w_out = w_out;
+  if (int rc = run_experts<T>(s, hidden, w, sh, L, ws, out, status, sms, st, &dr)) return rc;
+  return run_combine<T>(s, L, ws, at<float>(ws, L.topw), w.kind == TARFA_W_INT4, sh != nullptr,
+                        false, out, st, true);
+}
+
 extern "C" {
 
 int tarfa_b200_abi_version(void) { return TARFA_B200_ABI_VERSION; }
@@ -757,6 +883,14 @@ int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
                                     top_idx_out, top_w_out, L, workspace, status, sms, st);
     if (!rc) stage_mark(4, st);
     return rc;
+  }
+  if (use_decode_routing(s, *weights)) {
+    return s.dtype == TARFA_BF16
+               ? run_decode_layer<__nv_bfloat16>(s, hidden, router_weight, router_bias, *weights,
+                                                 sh, out, top_idx_out, top_w_out, L, workspace,
+                                                 status, sms, st)
+               : run_decode_layer<__half>(s, hidden, router_weight, router_bias, *weights, sh, out,
+                                          top_idx_out, top_w_out, L, workspace, status, sms, st);
   }
   if (s.dtype == TARFA_BF16) {
     rc = launch_router<__nv_bfloat16>(s, hidden, router_weight, router_bias,

@@ -21,6 +21,7 @@ template <> struct Elem<__nv_bfloat16> {
   TARFA_DEVI static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
   TARFA_DEVI static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
   TARFA_DEVI static float bits_to_f(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+  TARFA_DEVI static uint16_t to_bits(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
   // bf16 0x4300 = 128.0 with a 7-bit mantissa: 0x4300 | q == 128 + q exactly
   static constexpr uint32_t kMagic = 0x43004300u;
   static constexpr uint32_t kMagicMinus8 = 0x43084308u;  // 136.0 in both halves
@@ -31,6 +32,7 @@ template <> struct Elem<__half> {
   TARFA_DEVI static float to_f(__half v) { return __half2float(v); }
   TARFA_DEVI static __half from_f(float v) { return __float2half_rn(v); }
   TARFA_DEVI static float bits_to_f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+  TARFA_DEVI static uint16_t to_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
   // fp16 0x6400 = 1024.0 with a 10-bit mantissa: 0x6400 | q == 1024 + q exactly
   static constexpr uint32_t kMagic = 0x64006400u;
   static constexpr uint32_t kMagicMinus8 = 0x64086408u;  // 1032.0 in both halves
@@ -141,6 +143,13 @@ template <typename T> TARFA_DEVI uint32_t nib_pair(uint32_t w, int s) {
 // ---------------------------------------------------------------------------
 constexpr unsigned kStatusBadExpert = 1u;    // TARFA_DEV_BAD_EXPERT_ID
 constexpr unsigned kStatusWaitTimeout = 2u;  // TARFA_DEV_WAIT_TIMEOUT
+
+// Programmatic dependent launch.  launch_dependents lets the next kernel of the
+// stream (launched with programmatic stream serialization) be scheduled before
+// this one ends; grid_dep_wait blocks until the previous kernel has completed
+// and its memory is visible.  Both are no-ops without the launch attribute.
+TARFA_DEVI void grid_dep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+TARFA_DEVI void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 TARFA_DEVI void raise_status(unsigned* status, unsigned bit) {
   if (status) atomicOr(status, bit);

@@ -11,7 +11,7 @@
 //               ring, K split across the 8 warps and reduced in a fixed order
 //   warp 9      aux: router rows (phase 0)
 //
-//   phase 0  router logits (exact, fp64-accumulated; aux warps) || shared
+//   phase 0  router logits (exact, exact.cuh; aux warps) || shared
 //            expert gate/up (independent of the routing; producer/consumers)
 //   barrier  grid-wide, bounded spin
 //   phase 1  every CTA computes the top-k and the expert-sorted unit table for
@@ -522,24 +522,8 @@ TARFA_DEVI void router_row(const Args& a, int row) {
   }
   for (int t = 0; t < a.T; ++t) {
     const T* xrow = static_cast<const T*>(a.h) + (int64_t)t * a.H;
-    double part[4] = {0.0, 0.0, 0.0, 0.0};
-#pragma unroll
-    for (int j = 0; j < MAXC; ++j) {
-      const int ch = lane + 32 * j;
-      if (ch < nch) {
-        const uint4 xv = ld_cached(xrow + ch * 8);
-        const T* wp = reinterpret_cast<const T*>(&wv[j]);
-        const T* xp = reinterpret_cast<const T*>(&xv);
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          part[q & 3] += (double)__fmul_rn(Elem<T>::to_f(wp[q]), Elem<T>::to_f(xp[q]));
-      }
-    }
-    double acc = (part[0] + part[1]) + (part[2] + part[3]);
-#pragma unroll
-    for (int d = 16; d; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+    float lgv = row_dot_exact<T, MAXC>(wv, wrow, xrow, a.H);
     if (lane == 0) {
-      float lgv = Elem<T>::to_f(round_from_f64<T>(acc));
       if (row < a.E) {
         if (a.bias) lgv = rnd<T>(lgv + Elem<T>::to_f(static_cast<const T*>(a.bias)[row]));
         a.logits[(int64_t)t * a.E + row] = lgv;
@@ -641,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const Args a)
   for (int t = wi; t < a.T; t += kConsumers + 1) {
     int64_t* io = (blockIdx.x == 0 && a.idx_out) ? a.idx_out + (int64_t)t * a.K : nullptr;
     float* wo = (blockIdx.x == 0 && a.w_out) ? a.w_out + (int64_t)t * a.K : nullptr;
-    warp_topk(a.logits + (int64_t)t * a.E, a.E, a.K, s.idx + t * a.K, s.w + t * a.K, io, wo);
+    warp_topk<T>(a.logits + (int64_t)t * a.E, a.E, a.K, s.idx + t * a.K, s.w + t * a.K, io, wo);
   }
   group_barrier(1, kWorkThreads);
   for (int r = tid; r < R; r += nthr) {     // route r = k*T + t

@@ -25,6 +25,7 @@
 // token vector is byte-permuted the same way.
 #pragma once
 #include "common.cuh"
+#include "routing.cuh"
 
 namespace tarfa {
 
@@ -36,15 +37,6 @@ enum GemvPhase { kGateUp = 0, kDown = 1 };
 // kModeInt4Dequant: int4 dequantised to the model dtype, then the exact path
 //   (fused_int4.py:254-260 with channel_q4.py:10-14).
 enum GemvMode { kModeExact = 0, kModeInt4Fused = 1, kModeInt4Dequant = 2 };
-
-// Unit table written by the permute stage:
-//   hdr[0] routed units, hdr[1] routed rows, hdr[2] has shared unit, hdr[3] shared row0
-//   desc[u] = {expert, row0, nrows, 0}; routed units in ascending expert id,
-//   the shared unit (expert == E) last.
-struct UnitDesc { int expert, row0, nrows, pad; };
-TARFA_DEVI const UnitDesc* unit_descs(const int32_t* units) {
-  return reinterpret_cast<const UnitDesc*>(units + 4);
-}
 
 struct GemvArgs {
   const void* x;             // GATE_UP: hidden [T, ld_x]; DOWN: act [R, ld_x]
@@ -67,6 +59,12 @@ struct GemvArgs {
   void* out;                 // GATE_UP: act (model dtype); DOWN: y (fp32)
   int64_t ld_out;
   unsigned* status;
+  // 0: unit table from `units` (written by an earlier kernel);
+  // 1: route in the kernel from route.logits (decode GATE_UP, routing.cuh);
+  // 2: shared unit only, at its fixed rows (decode GATE_UP of the dense shared
+  //    expert beside int4 routed experts)
+  int route_mode;
+  DecodeRoute route;
 };
 
 constexpr int kGemvThreads = 256;
@@ -218,21 +216,42 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   constexpr int kGroups = kGemvWarps / KSPLIT;              // tiles per CTA step
   constexpr int TR = PHASE == kGateUp ? 8 : 16;             // tile rows per unit index
   __shared__ float red[kGroups][KSPLIT][NTB * 4][32];
+  extern __shared__ int gemv_smem[];                        // routing (route_mode 1)
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int grp = warp / KSPLIT, kw = warp % KSPLIT;
   const int g = lane >> 2, c = lane & 3;
 
-  const int32_t* hdr = a.units;
-  const int nu = hdr[0];
-  const int has_sh = hdr[2];
-  const UnitDesc* descs = unit_descs(a.units);
+  grid_dep_launch_dependents();
+  const int32_t* units = a.units;
+  const int32_t* perm_tok = a.perm_tok;
+  int nu = -1;          // routed units; unknown until routed (route_mode 1)
+  bool has_sh;
+  if (a.route_mode == 0) {
+    grid_dep_wait();
+    nu = units[0];
+    has_sh = units[2] != 0;
+  } else {
+    has_sh = a.route.add_shared != 0;
+    if (a.route_mode == 2) nu = 0;
+  }
+  // the shared unit's rows are fixed when the routing is the router's own top-k
+  const UnitDesc fixed_sh{a.E, a.route.T * a.route.K, a.route.T, 0};
   const int tiles_r = a.N_r / TR, tiles_s = a.N_s / TR;
-  const int nt_r = (a.which & 1) ? nu * tiles_r : 0;
+  // shared-expert tiles first: they need no routing, so with in-kernel routing
+  // they run while the router kernel is still finishing
   const int nt_s = (!INT4 && (a.which & 2) && has_sh) ? tiles_s : 0;
-  const int ntiles = nt_r + nt_s;
 
-  for (int base = blockIdx.x * kGroups; base < ntiles; base += gridDim.x * kGroups) {
+  for (int base = blockIdx.x * kGroups;; base += gridDim.x * kGroups) {
+    if (nu < 0 && base + kGroups > nt_s) {   // CTA-uniform: first step with a routed tile
+      const RouteSmem m = cta_route<T>(a.route, a.E, gemv_smem, a.status);
+      units = m.units;
+      perm_tok = m.perm_tok;
+      nu = units[0];
+    }
+    const int nt_r = ((a.which & 1) && nu > 0) ? nu * tiles_r : 0;
+    const int ntiles = nt_s + nt_r;
+    if (base >= ntiles) break;
     const int tile = base + grp;
     if (tile >= ntiles) continue;   // uniform within a warp group; groups sync separately
     // -------- resolve the tile ------------------------------------------------
@@ -243,10 +262,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
     const char* rowB = nullptr;   // weight row for fragment rows g+8
     const T* scA = nullptr;       // int4 scale rows
     const T* scB = nullptr;
-    if (tile < nt_r) {
-      const int u = tile / tiles_r;
-      tt = tile % tiles_r;
-      d = descs[u];
+    if (tile >= nt_s) {
+      const int u = (tile - nt_s) / tiles_r;
+      tt = (tile - nt_s) % tiles_r;
+      d = unit_descs(units)[u];
       const int slot = a.expert_slot ? a.expert_slot[d.expert] : d.expert;
       K = a.K_r;
       const int ra = PHASE == kGateUp ? tt * 8 + g : tt * 16 + g;
@@ -262,8 +281,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
       }
     } else {
       shared_unit = true;
-      tt = tile - nt_r;
-      d = descs[nu];
+      tt = tile;
+      d = a.route_mode != 0 ? fixed_sh : unit_descs(units)[nu];
       K = a.K_s;
       const T* s0 = static_cast<const T*>(a.sw0);
       if (PHASE == kGateUp) {
@@ -274,7 +293,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
         rowB = reinterpret_cast<const char*>(s0 + (int64_t)(tt * 16 + g + 8) * K);
       }
     }
-    (void)shared_unit;
     const int ntok = d.nrows;
     const int ntb_groups = (ntok + 8 * NTB - 1) / (8 * NTB);
 
@@ -293,7 +311,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
         xrow[b] = nullptr;
         if (n < ntok) {
           const int r = d.row0 + n;
-          const int xr = PHASE == kGateUp ? a.perm_tok[r] : r;
+          // shared-unit rows hold the tokens in order (perm_tok[row0 + n] == n)
+          const int xr = PHASE == kGateUp ? (shared_unit ? n : perm_tok[r]) : r;
           xrow[b] = reinterpret_cast<const char*>(static_cast<const T*>(a.x) + (int64_t)xr * a.ld_x);
         }
       }
@@ -367,6 +386,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
       }
     }
   }
+  // a kernel that never waited still completes only after its predecessor, so
+  // that the next kernel's wait covers the whole chain
+  if (a.route_mode == 2) grid_dep_wait();
 }
 
 }  // namespace tarfa

@@ -1,0 +1,329 @@
+// Routing primitives shared by the router, permute and decode GEMV kernels:
+// the unit table, the stable counting-sort permute, and the warp top-k.
+//
+// Permute (fused_int4.py:228-229, 241): routes r = k*T + t are stably sorted
+// by expert id, giving per expert the (k-slot, token) row-major order of
+// torch.where(one_hot(idx).permute(2,1,0)[e]).
+#pragma once
+#include "common.cuh"
+
+namespace tarfa {
+
+// Unit table written by the permute stage:
+//   hdr[0] routed units, hdr[1] routed rows, hdr[2] has shared unit, hdr[3] shared row0
+//   desc[u] = {expert, row0, nrows, 0}; routed units in ascending expert id,
+//   the shared unit (expert == E) last.
+struct UnitDesc { int expert, row0, nrows, pad; };
+TARFA_DEVI const UnitDesc* unit_descs(const int32_t* units) {
+  return reinterpret_cast<const UnitDesc*>(units + 4);
+}
+
+struct PermuteOut {
+  int32_t* seg_offsets;   // [E+1] or null
+  int32_t* perm_tok;      // [R_total]: row -> token
+  int32_t* perm_slot;     // [T*K] or null: row -> k-slot
+  int32_t* route_row;     // [T*K] or null: (t, k) -> row, -1 for a skipped route
+  int32_t* units;         // unit table (header + UnitDesc[])
+  int32_t* idx32;         // [T*K] or null: int32 copy of the expert ids
+};
+
+// Shared-memory ints needed by block_permute.
+__host__ __device__ inline size_t permute_smem_ints(int nwarps, int E) {
+  return (size_t)nwarps * E + E;
+}
+
+// Block-cooperative stable counting sort of T*K routes by expert id.
+// Any blockDim that is a multiple of 32; E <= smem budget.
+template <typename Idx>
+__device__ void block_permute(const Idx* idx, int T, int K, int E, bool add_shared,
+                              const PermuteOut& o, int* smem, unsigned* status) {
+  const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = T * K;
+  int* wcnt = smem;            // [nw][E] per-warp counts, then running cursors
+  int* off = smem + nw * E;    // [E] totals, then segment offsets
+  for (int i = threadIdx.x; i < nw * E + E; i += blockDim.x) smem[i] = 0;
+  __syncthreads();
+  const int r0 = (int)((int64_t)R * warp / nw), r1 = (int)((int64_t)R * (warp + 1) / nw);
+  for (int r = r0 + lane; r < r1; r += 32) {
+    const int t = r % T, k = r / T;
+    const int64_t e = (int64_t)idx[(int64_t)t * K + k];
+    if (e >= 0 && e < E) atomicAdd(&wcnt[warp * E + (int)e], 1);
+    else if (e != E) raise_status(status, kStatusBadExpert);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int s = 0;
+    for (int w = 0; w < nw; ++w) {
+      const int cnt = wcnt[w * E + e];
+      wcnt[w * E + e] = s;
+      s += cnt;
+    }
+    off[e] = s;
+  }
+  __syncthreads();
+  UnitDesc* descs = reinterpret_cast<UnitDesc*>(o.units + 4);
+  if (warp == 0) {
+    const int per = (E + 31) / 32;
+    const int b0 = min(lane * per, E), b1 = min(b0 + per, E);
+    int s = 0, nz = 0;
+    for (int e = b0; e < b1; ++e) { s += off[e]; nz += off[e] > 0; }
+    int ps = s, pnz = nz;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, ps, d);
+      const int y = __shfl_up_sync(0xffffffffu, pnz, d);
+      if (lane >= d) { ps += x; pnz += y; }
+    }
+    int es = ps - s, enz = pnz - nz;
+    const int rows = __shfl_sync(0xffffffffu, ps, 31), nunits = __shfl_sync(0xffffffffu, pnz, 31);
+    for (int e = b0; e < b1; ++e) {
+      const int cnt = off[e];
+      if (cnt > 0) { descs[enz] = UnitDesc{e, es, cnt, 0}; ++enz; }
+      if (o.seg_offsets) o.seg_offsets[e] = es;
+      off[e] = es;
+      es += cnt;
+    }
+    if (lane == 0) {
+      if (o.seg_offsets) o.seg_offsets[E] = rows;
+      o.units[0] = nunits;
+      o.units[1] = rows;
+      o.units[2] = add_shared ? 1 : 0;
+      o.units[3] = rows;
+      if (add_shared) descs[nunits] = UnitDesc{E, rows, T, 0};
+    }
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+  for (int rb = r0; rb < r1; rb += 32) {
+    const int r = rb + lane;
+    const bool in = r < r1;
+    const int t = in ? r % T : 0, k = in ? r / T : 0;
+    const int64_t e64 = in ? (int64_t)idx[(int64_t)t * K + k] : -1;
+    const bool routed = in && e64 >= 0 && e64 < E;
+    const int e = routed ? (int)e64 : 0;
+    if (in && o.idx32) o.idx32[t * K + k] = (int32_t)e64;
+    const unsigned peers = __match_any_sync(0xffffffffu, routed ? e : -1 - lane);
+    const int rank = __popc(peers & lt);
+    const int cur = routed ? wcnt[warp * E + e] : 0;
+    __syncwarp();
+    if (routed && rank == 0) wcnt[warp * E + e] = cur + __popc(peers);
+    __syncwarp();
+    if (routed) {
+      const int row = off[e] + cur + rank;
+      o.perm_tok[row] = t;
+      if (o.perm_slot) o.perm_slot[row] = k;
+      if (o.route_row) o.route_row[t * K + k] = row;
+    } else if (in && o.route_row) {
+      o.route_row[t * K + k] = -1;
+    }
+  }
+  __syncthreads();
+  const int rows = o.units[1];
+  if (add_shared)
+    for (int t = threadIdx.x; t < T; t += blockDim.x) o.perm_tok[rows + t] = t;
+  if (o.perm_slot)   // rows past the routed ones (skipped routes) are marked -1
+    for (int r = rows + threadIdx.x; r < R; r += blockDim.x) {
+      o.perm_slot[r] = -1;
+      if (!add_shared) o.perm_tok[r] = -1;
+    }
+}
+
+// Orderable 32-bit key of a model-dtype logit and its expert id (E <= 65535):
+// larger logit first, then smaller id; -0 and +0 compare equal.
+template <typename T>
+TARFA_DEVI uint32_t topk_key32(float v, int e) {
+  uint32_t u = Elem<T>::to_bits(v);
+  if ((u & 0x7FFFu) == 0) u = 0;
+  u = (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
+  return (u << 16) | (0xFFFFu - (uint32_t)e);
+}
+
+template <typename T>
+TARFA_DEVI float key32_value(uint32_t key) {
+  uint32_t u = key >> 16;
+  u = (u & 0x8000u) ? (u & 0x7FFFu) : (~u & 0xFFFFu);
+  return Elem<T>::bits_to_f((uint16_t)u);
+}
+
+// One warp: softmax + top-k over E <= 32 * NPL logits of one token (values in
+// the model dtype, held as fp32).  Selection is a warp max-reduction
+// (redux.sync) of 32-bit keys per step; only the lane that owned the winner
+// rescans its NPL keys.  idx_smem (optional) receives the ids as well.
+template <typename T, int NPL>
+TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float* topw,
+                            int64_t* idx_out, float* w_out, int32_t* idx_smem) {
+  const int lane = threadIdx.x & 31;
+  uint32_t key[NPL];
+  uint32_t best = 0;
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    const int e = j * 32 + lane;
+    key[j] = e < E ? topk_key32<T>(__ldcg(lg + e), e) : 0u;
+    best = max(best, key[j]);
+  }
+  const float m = key32_value<T>(__reduce_max_sync(0xffffffffu, best));
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < NPL; ++j)
+    if (j * 32 + lane < E) s += expf(key32_value<T>(key[j]) - m);
+#pragma unroll
+  for (int d = 16; d; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+  int my_e = 0;
+  float my_v = 0.f;
+  for (int k = 0; k < K; ++k) {
+    const uint32_t kk = __reduce_max_sync(0xffffffffu, best);
+    const int e = (int)(0xFFFFu - (kk & 0xFFFFu));
+    if (lane == k) { my_e = e; my_v = key32_value<T>(kk); }
+    if ((e & 31) == lane) {
+      best = 0;
+#pragma unroll
+      for (int j = 0; j < NPL; ++j) {
+        if (j == (e >> 5)) key[j] = 0u;
+        best = max(best, key[j]);
+      }
+    }
+  }
+  // softmax probabilities of the selected (fp32), renormalised over the k
+  // (modeling_qwen3_5_moe.py:766-768); K <= 32
+  const float p = lane < K ? __fdiv_rn(expf(my_v - m), s) : 0.f;
+  float vs = 0.f;
+  for (int k = 0; k < K; ++k) vs = __fadd_rn(vs, __shfl_sync(0xffffffffu, p, k));
+  if (lane < K) {
+    const float w = __fdiv_rn(p, vs);
+    idx32[lane] = my_e;
+    topw[lane] = w;
+    if (idx_out) idx_out[lane] = my_e;
+    if (w_out) w_out[lane] = w;
+    if (idx_smem) idx_smem[lane] = my_e;
+  }
+}
+
+template <typename T>
+TARFA_DEVI void warp_topk(const float* lg, int E, int K, int32_t* idx32, float* topw,
+                          int64_t* idx_out, float* w_out, int32_t* idx_smem = nullptr) {
+  if (E <= 256) warp_topk_n<T, 8>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
+  else warp_topk_n<T, 32>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
+}
+
+// Permute for one token whose K routes name K distinct experts (the router's
+// own top-k): rows in ascending expert id, one unit per route, shared unit
+// last.  Same outputs as block_permute for that case.  One warp.
+TARFA_DEVI void warp_permute_one_token(const int32_t* idx, int K, int E, bool add_shared,
+                                       const PermuteOut& o) {
+  const int lane = threadIdx.x & 31;
+  const int e = lane < K ? idx[lane] : 0x7fffffff;
+  int rank = 0;
+  for (int j = 0; j < K; ++j) rank += __shfl_sync(0xffffffffu, e, j) < e;
+  UnitDesc* descs = reinterpret_cast<UnitDesc*>(o.units + 4);
+  if (lane < K) {
+    descs[rank] = UnitDesc{e, rank, 1, 0};
+    o.perm_tok[rank] = 0;
+    if (o.perm_slot) o.perm_slot[rank] = lane;
+    if (o.route_row) o.route_row[lane] = rank;
+    if (o.idx32) o.idx32[lane] = e;
+  }
+  if (lane == 0) {
+    o.units[0] = K;
+    o.units[1] = K;
+    o.units[2] = add_shared ? 1 : 0;
+    o.units[3] = K;
+    if (add_shared) {
+      descs[K] = UnitDesc{E, K, 1, 0};
+      o.perm_tok[K] = 0;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// in-kernel routing for decode batches
+// ---------------------------------------------------------------------------
+// The decode GEMV computes top-k and permute itself, in every CTA, from the
+// logits the router kernel wrote: no serial tail in the router, and the
+// routing of a few tokens costs one L2 read and ~1 us of warp work per CTA.
+// CTA 0 also writes the global copies the later kernels read.
+//
+// The router's own top-k names K distinct valid experts per token, so the
+// routed rows are exactly T*K and the shared-expert unit is fixed before the
+// routing is known: rows [T*K, T*K + T), token t at row T*K + t.
+struct DecodeRoute {
+  const float* logits;   // [T, E] correctly rounded logits (+ bias) from the router kernel
+  int T, K;
+  int add_shared;
+  int32_t* g_units;      // global copies for the kernels that follow (written by CTA 0)
+  int32_t* g_perm_tok;
+  int32_t* g_perm_slot;
+  int32_t* g_route_row;
+  int32_t* g_idx32;
+  float* g_topw;
+  int64_t* idx_out;      // optional user outputs
+  float* w_out;
+};
+
+// Shared-memory ints cta_route needs (a multiple of 4, so what follows stays 16-byte aligned).
+__host__ __device__ inline int route_smem_ints(int T, int K, int E, int nwarps) {
+  const int R = T * K, Umax = (R < E ? R : E);
+  const int n = 2 * R + (4 + 4 * (Umax + 1)) + (R + T) + 2 * R +
+                (T > 1 ? (int)permute_smem_ints(nwarps, E) : 0);
+  return (n + 3) & ~3;
+}
+
+struct RouteSmem {
+  int32_t* idx;
+  float* topw;
+  int32_t* units;
+  int32_t* perm_tok;
+  int32_t* perm_slot;
+  int32_t* route_row;
+  int* scratch;
+};
+
+TARFA_DEVI RouteSmem route_smem_carve(int* smem, int T, int K, int E) {
+  const int R = T * K, Umax = (R < E ? R : E);
+  RouteSmem m;
+  m.idx = smem;
+  m.topw = reinterpret_cast<float*>(smem + R);
+  m.units = smem + 2 * R;
+  m.perm_tok = m.units + 4 + 4 * (Umax + 1);
+  m.perm_slot = m.perm_tok + R + T;
+  m.route_row = m.perm_slot + R;
+  m.scratch = m.route_row + R;
+  return m;
+}
+
+// CTA-wide: wait for the router kernel, top-k every token, permute into shared
+// memory; CTA 0 publishes the global copies.  All threads must call it.
+template <typename T>
+__device__ RouteSmem cta_route(const DecodeRoute& r, int E, int* smem, unsigned* status) {
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const RouteSmem m = route_smem_carve(smem, r.T, r.K, E);
+  const bool pub = blockIdx.x == 0;
+  grid_dep_wait();
+  for (int t = warp; t < r.T; t += nw)
+    warp_topk<T>(r.logits + (int64_t)t * E, E, r.K, m.idx + t * r.K, m.topw + t * r.K,
+                 pub && r.idx_out ? r.idx_out + (int64_t)t * r.K : nullptr,
+                 pub && r.w_out ? r.w_out + (int64_t)t * r.K : nullptr, nullptr);
+  __syncthreads();
+  const PermuteOut o{nullptr, m.perm_tok, m.perm_slot, m.route_row, m.units, nullptr};
+  if (r.T == 1) {
+    if (warp == 0) warp_permute_one_token(m.idx, r.K, E, r.add_shared != 0, o);
+  } else {
+    block_permute<int32_t>(m.idx, r.T, r.K, E, r.add_shared != 0, o, m.scratch, status);
+  }
+  __syncthreads();
+  if (pub) {
+    const int R = r.T * r.K;
+    const int nunits = m.units[0] + (m.units[2] ? 1 : 0);
+    for (int i = threadIdx.x; i < 4 + 4 * nunits; i += blockDim.x) r.g_units[i] = m.units[i];
+    for (int i = threadIdx.x; i < R + (r.add_shared ? r.T : 0); i += blockDim.x)
+      r.g_perm_tok[i] = m.perm_tok[i];
+    for (int i = threadIdx.x; i < R; i += blockDim.x) {
+      r.g_perm_slot[i] = m.perm_slot[i];
+      r.g_route_row[i] = m.route_row[i];
+      r.g_idx32[i] = m.idx[i];
+      r.g_topw[i] = m.topw[i];
+    }
+  }
+  return m;
+}
+
+}  // namespace tarfa
