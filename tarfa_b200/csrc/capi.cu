@@ -647,8 +647,11 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
 // Decode batches on the GEMV path route inside the gate_up kernel (routing.cuh):
 // the router kernel only writes logits, and the expert kernels are programmatic
 // dependents of one another.
+std::atomic<int64_t> g_decode_routing_max_tokens{16};
+
 bool use_decode_routing(const tarfa_moe_shape& s, const tarfa_moe_weights& w) {
-  return s.tokens <= 16 && s.tokens * s.top_k <= 128 && s.experts <= 1024 &&
+  return s.tokens <= g_decode_routing_max_tokens.load() && s.tokens <= 16 &&
+         s.tokens * s.top_k <= 128 && s.experts <= 1024 &&
          !use_gemm(s, w, s.shared_inter) && !use_fused_decode(s, w);
 }
 
@@ -733,6 +736,13 @@ size_t tarfa_b200_workspace_size(const tarfa_moe_shape* shape, int32_t op) {
 int tarfa_b200_set_fused_decode_max_tokens(int64_t tokens) {
   if (tokens < 0) return fail(TARFA_ERR_INVALID, "fused_decode_max_tokens %lld < 0", (long long)tokens);
   g_fused_max_tokens.store(tokens);
+  return TARFA_OK;
+}
+
+int tarfa_b200_set_decode_routing_max_tokens(int64_t tokens) {
+  if (tokens < 0)
+    return fail(TARFA_ERR_INVALID, "decode_routing_max_tokens %lld < 0", (long long)tokens);
+  g_decode_routing_max_tokens.store(tokens);
   return TARFA_OK;
 }
 

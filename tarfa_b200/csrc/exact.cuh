@@ -15,6 +15,7 @@
 //             correctly rounded result (rounding is monotonic).  B is about
 //             2^-17 of sum|e| ~ 2^-41 of the logit, so this fails for ~1e-7 of
 //             all logits, and for exact ties reached through rounded sums.
+//             The check runs in fp32 (exact_round).
 // slow path   An exact integer sum: every product is m_w * m_x * 2^(e_w + e_x)
 //             with integer significands; a 576-bit two's complement
 //             fixed-point accumulator (LSB 2^-266, the smallest product of two
@@ -69,25 +70,34 @@ TARFA_DEVI void exact_warp_reduce(ExactAcc& x) {
   }
 }
 
-// Correct rounding from a reduced accumulator.  depth = the longest chain of
-// additions into c (terms per lane + 2 per merge level).  Returns false when
-// the bound does not decide the rounding, or the result is zero (its sign is
-// then decided by the exact slow path: +0 for an exact zero).
+// Correct rounding from a reduced accumulator, in fp32 only.  depth = the
+// longest chain of additions into c (terms per lane + 2 per merge level).
+// f + g == s + c exactly (TwoSum); v = the model-dtype rounding of f.  The
+// exact dot product lies within B of f + g; when both rounding midpoints
+// around v are farther than B from f + g, v is its correct rounding.
+// (mu - f and f - md are exact: f lies between the midpoints, within a factor
+// of two of each.)  Returns false when that does not decide, or when v is zero
+// (sign undecided: +0 for an exact zero) or not finite; the exact slow path
+// then decides.
 template <typename T>
 TARFA_DEVI bool exact_round(const ExactAcc& x, int depth, float* out) {
-  const double X = (double)x.s + (double)x.c;
-  if (!isfinite(X)) {                 // inf / nan inputs: nothing to decide
-    *out = Elem<T>::to_f(Elem<T>::from_f(__fadd_rn(x.s, x.c)));
-    return true;
-  }
-  // gamma_D / (1 - gamma_D) <= 1.01 * D * 2^-24 for D < 2^14; 2^-130 covers
-  // products that underflowed fp32; 2^-50 |X| the fp64 sums below.
-  const double B = 1.01 * (double)depth * 0x1p-24 * (double)x.a + 0x1p-130 + 0x1p-50 * fabs(X);
-  const float lo = Elem<T>::to_f(round_from_f64<T>(X - B));
-  const float hi = Elem<T>::to_f(round_from_f64<T>(X + B));
-  *out = lo;
-  // a result of zero has an undecided sign (exact zero is +0, tiny negatives -0)
-  return lo == hi && lo != 0.f;
+  const float f = __fadd_rn(x.s, x.c);
+  const float z = __fsub_rn(f, x.s);
+  const float g = __fadd_rn(__fsub_rn(x.s, __fsub_rn(f, z)), __fsub_rn(x.c, z));
+  const float v = Elem<T>::to_f(Elem<T>::from_f(f));
+  *out = v;
+  if (!isfinite(f)) return true;                 // inf / nan inputs: nothing to decide
+  if (v == 0.f || !isfinite(v)) return false;
+  // gamma_D / (1 - gamma_D) <= 1.02 * D * 2^-24 covers the sum of the errors and
+  // its own rounding; 2^-126 covers products that underflowed fp32
+  const float B = fmaf(1.02f * (float)depth * 0x1p-24f, x.a, 0x1p-126f);
+  const uint16_t b = Elem<T>::to_bits(v);
+  const float vu = Elem<T>::bits_to_f((uint16_t)(v > 0.f ? b + 1 : b - 1));   // next larger
+  const float vd = Elem<T>::bits_to_f((uint16_t)(v > 0.f ? b - 1 : b + 1));   // next smaller
+  const float mu = 0.5f * (v + vu), md = 0.5f * (v + vd);                     // exact
+  const float du = __fsub_rn(__fsub_rn(mu, f), g);
+  const float dd = __fadd_rn(__fsub_rn(f, md), g);
+  return du > B && dd > B;
 }
 
 // ---------------------------------------------------------------------------
@@ -227,8 +237,7 @@ __device__ __noinline__ float warp_exact_dot(const T* a, const T* b, int H) {
 }
 
 // Finish a warp's two accumulators into the correctly rounded value; lane 0
-// decides for the warp (lanes may differ in c after the butterfly, and the
-// fp64 check costs 32x less on one lane).  chains =
+// decides for the warp (lanes may differ in c after the butterfly).  chains =
 // terms in the longer per-lane chain.  Falls back to the exact integer sum.
 template <typename T>
 TARFA_DEVI float exact_finish(ExactAcc x0, const ExactAcc& x1, int chains, const T* a, const T* b,
@@ -237,7 +246,7 @@ TARFA_DEVI float exact_finish(ExactAcc x0, const ExactAcc& x1, int chains, const
   exact_warp_reduce(x0);
   float v = 0.f;
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = exact_round<T>(x0, chains + 2 + 10, &v);   // fp64: one lane
+  if ((threadIdx.x & 31) == 0) ok = exact_round<T>(x0, chains + 2 + 10, &v);
   ok = __shfl_sync(0xffffffffu, ok, 0);
   v = __shfl_sync(0xffffffffu, v, 0);
   if (!ok) v = warp_exact_dot<T>(a, b, H);

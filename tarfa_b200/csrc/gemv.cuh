@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
 
   for (int base = blockIdx.x * kGroups;; base += gridDim.x * kGroups) {
     if (nu < 0 && base + kGroups > nt_s) {   // CTA-uniform: first step with a routed tile
-      const RouteSmem m = cta_route<T>(a.route, a.E, gemv_smem, a.status);
+      const RouteSmem m = cta_route<T, (NTB > 1)>(a.route, a.E, gemv_smem, a.status);
       units = m.units;
       perm_tok = m.perm_tok;
       nu = units[0];

@@ -198,11 +198,20 @@ TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float
   }
 }
 
+// The 32-keys-per-lane variant is not inlined: its registers stay out of the
+// callers' hot loops (the decode GEMV inlines the routing).
+template <typename T>
+__device__ __noinline__ void warp_topk_wide(const float* lg, int E, int K, int32_t* idx32,
+                                            float* topw, int64_t* idx_out, float* w_out,
+                                            int32_t* idx_smem) {
+  warp_topk_n<T, 32>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
+}
+
 template <typename T>
 TARFA_DEVI void warp_topk(const float* lg, int E, int K, int32_t* idx32, float* topw,
                           int64_t* idx_out, float* w_out, int32_t* idx_smem = nullptr) {
   if (E <= 256) warp_topk_n<T, 8>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
-  else warp_topk_n<T, 32>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
+  else warp_topk_wide<T>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
 }
 
 // Permute for one token whose K routes name K distinct experts (the router's
@@ -290,14 +299,11 @@ TARFA_DEVI RouteSmem route_smem_carve(int* smem, int T, int K, int E) {
   return m;
 }
 
-// CTA-wide: wait for the router kernel, top-k every token, permute into shared
-// memory; CTA 0 publishes the global copies.  All threads must call it.
+// Top-k of every token and permute into shared memory (all threads of the CTA).
 template <typename T>
-__device__ RouteSmem cta_route(const DecodeRoute& r, int E, int* smem, unsigned* status) {
+TARFA_DEVI void cta_route_body(const DecodeRoute& r, int E, const RouteSmem& m, unsigned* status) {
   const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const RouteSmem m = route_smem_carve(smem, r.T, r.K, E);
   const bool pub = blockIdx.x == 0;
-  grid_dep_wait();
   for (int t = warp; t < r.T; t += nw)
     warp_topk<T>(r.logits + (int64_t)t * E, E, r.K, m.idx + t * r.K, m.topw + t * r.K,
                  pub && r.idx_out ? r.idx_out + (int64_t)t * r.K : nullptr,
@@ -310,7 +316,27 @@ __device__ RouteSmem cta_route(const DecodeRoute& r, int E, int* smem, unsigned*
     block_permute<int32_t>(m.idx, r.T, r.K, E, r.add_shared != 0, o, m.scratch, status);
   }
   __syncthreads();
-  if (pub) {
+}
+
+template <typename T>
+__device__ __noinline__ void cta_route_call(const DecodeRoute& r, int E, const RouteSmem& m,
+                                            unsigned* status) {
+  cta_route_body<T>(r, E, m, status);
+}
+
+// CTA-wide: wait for the router kernel, top-k every token, permute into shared
+// memory; CTA 0 publishes the global copies.  All threads must call it.
+// CALL: run the routing as a separate (not inlined) function.  The GEMV's hot
+// loop is sensitive to the code around it: measured on the config-1 layer,
+// inlining is faster for the one-token-block kernels (T <= 8: 53 vs 57 us at
+// T = 1) and a call faster for the two-block kernels (T = 16: 375 vs 420 us).
+template <typename T, bool CALL>
+TARFA_DEVI RouteSmem cta_route(const DecodeRoute& r, int E, int* smem, unsigned* status) {
+  const RouteSmem m = route_smem_carve(smem, r.T, r.K, E);
+  grid_dep_wait();
+  if (CALL) cta_route_call<T>(r, E, m, status);
+  else cta_route_body<T>(r, E, m, status);
+  if (blockIdx.x == 0) {
     const int R = r.T * r.K;
     const int nunits = m.units[0] + (m.units[2] ? 1 : 0);
     for (int i = threadIdx.x; i < 4 + 4 * nunits; i += blockDim.x) r.g_units[i] = m.units[i];

@@ -347,6 +347,12 @@ def set_fused_decode_max_tokens(tokens: int) -> None:
     api.check(api.lib().tarfa_b200_set_fused_decode_max_tokens(int(tokens)))
 
 
+def set_decode_routing_max_tokens(tokens: int) -> None:
+    """``moe_layer`` routes batches of 1..``tokens`` (<= 16) inside the expert
+    GEMV; 0 uses the router kernel's own top-k (process-wide, default 16)."""
+    api.check(api.lib().tarfa_b200_set_decode_routing_max_tokens(int(tokens)))
+
+
 def set_stage_events(events) -> None:
     """Record ``events[i]`` (``torch.cuda.Event``) at layer stage boundary ``i``
     (0 start, 1 router/permute, 2 gate_up, 3 down, 4 combine) on this thread;
