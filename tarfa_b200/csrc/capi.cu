@@ -117,13 +117,15 @@ int noalloc_scratch(void** out) {
 // ---------------------------------------------------------------------------
 struct Ws {
   size_t counter, logits, gate_logit, idx32, topw, units, perm_tok, perm_slot, route_row, act, y,
-      xperm, bar, hb_cnt, wnorm;
+      xperm, bar, hb_cnt, wnorm, lgpart, phist, fxlist, fxcnt;
   size_t total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 constexpr size_t kZeroHeaderBytes = 2304;   // 16 + 16 + 8192/16*4, rounded to 256
+constexpr int64_t kRouterGemmMinTokens = 128;   // from here the router logits use the tensor cores
+constexpr int kRouterMaxSplit = 8;             // K splits of the tensor-core router GEMM
 
 Ws layout(const tarfa_moe_shape& s, int op) {
   const int64_t T = s.tokens, K = s.top_k, E = s.experts, H = s.hidden;
@@ -140,6 +142,7 @@ Ws layout(const tarfa_moe_shape& s, int op) {
   w.counter = 0;
   w.bar = 16;
   w.hb_cnt = 32;   // 8192 / 16 counters at most (hidden <= 8192)
+  w.fxcnt = 2096;  // router fix-up list length
   o = kZeroHeaderBytes;
   if (op == TARFA_OP_SHARED) {   // shared expert alone: one unit of T rows
     const int64_t Iss = s.shared_inter;
@@ -157,10 +160,16 @@ Ws layout(const tarfa_moe_shape& s, int op) {
   w.route_row = take(R * 4);
   w.perm_tok = take((Rt > 0 ? Rt : 1) * 4);
   w.perm_slot = take(R * 4);
+  w.phist = take((size_t)perm_blocks((int)R) * E * 4);   // multi-block permute histograms
   if (op == TARFA_OP_MOE_LAYER || op == TARFA_OP_ROUTER) {
     w.logits = take(T * E * 4);
     w.gate_logit = take(T * 4);
     w.wnorm = take(E * 4);
+    // fp32 partial logits of the tensor-core router (large batches only)
+    if (T >= kRouterGemmMinTokens) {
+      w.lgpart = take((size_t)kRouterMaxSplit * T * E * 4);
+      w.fxlist = take((size_t)T * (E + 1) * 4);   // logits to recompute exactly
+    }
   }
   if (op == TARFA_OP_MOE_LAYER || op == TARFA_OP_EXPERTS) {
     w.act = take(Rt * Imax * 2);
@@ -261,7 +270,6 @@ int launch_gemv_ntb(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStrea
 
 constexpr int kKsplitGateUp = 8;
 constexpr int kKsplitDown = 4;
-constexpr int64_t kRouterGemmMinTokens = 128;   // from here the router logits use the tensor cores
 
 // Token count from which dense layers take the tcgen05 grouped-GEMM path
 // (tarfa_b200_set_gemm_min_tokens); below it the tensor-core GEMV path.
@@ -492,6 +500,7 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
   const int tiles_dn = (Umax + (Is ? 1 : 0)) * (H / 16);
   if (!int4) {
     g.which = 3;
+
     rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st, pdl);
   } else {
     g.which = 1;
@@ -510,10 +519,9 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
   return TARFA_OK;
 }
 
-template <typename T>
-int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* top_w, bool int4,
-                bool with_shared, bool gemm_y, void* out, cudaStream_t st, bool pdl = false) {
-  const int T_ = (int)s.tokens, K = s.top_k, H = (int)s.hidden;
+CombineArgs make_combine_args(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* top_w,
+                              bool int4, bool with_shared, void* out) {
+  const int T_ = (int)s.tokens;
   CombineArgs c{};
   c.y = at<void>(ws, L.y);
   c.route_row = at<int32_t>(ws, L.route_row);
@@ -521,21 +529,27 @@ int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* to
   c.w = top_w;
   c.units = at<int32_t>(ws, L.units);
   c.T = T_;
-  c.K = K;
-  c.H = H;
+  c.K = s.top_k;
+  c.H = (int)s.hidden;
   c.E = (int)s.experts;
   c.order_router = T_ == 1;
   c.mode = !int4 ? kModeExact : (T_ == 1 ? kModeInt4Fused : kModeInt4Dequant);
   c.gate_logit = with_shared ? at<float>(ws, L.gate_logit) : nullptr;
   c.out = out;
-  if (T_ > 64) {   // large batch: one block per token, slot order sorted once
-    if (gemm_y) combine_token_kernel<T, T><<<T_, 256, 0, st>>>(c);   // GEMM path: y in model dtype
-    else combine_token_kernel<T, float><<<T_, 256, 0, st>>>(c);
-  } else {         // decode: thread per (token, column), many small blocks
-    const dim3 grid((H + 127) / 128, T_);
-    if (gemm_y) TARFA_CUDA(launch_k(combine_kernel<T, T>, grid, dim3(128), 0, st, pdl, c));
-    else TARFA_CUDA(launch_k(combine_kernel<T, float>, grid, dim3(128), 0, st, pdl, c));
-  }
+  return c;
+}
+
+template <typename T>
+int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* top_w, bool int4,
+                bool with_shared, bool gemm_y, void* out, cudaStream_t st, bool pdl = false) {
+  const int T_ = (int)s.tokens, H = (int)s.hidden;
+  const CombineArgs c = make_combine_args(s, L, ws, top_w, int4, with_shared, out);
+  // large batches: one block per token; decode: one-warp blocks, so that the
+  // few tokens' columns spread over many SMs (the loads are latency-bound)
+  const int threads = T_ > 64 ? kCombineTokenThreads : 32;
+  const dim3 grid(T_ > 64 ? 1 : (H / 8 + threads - 1) / threads, T_);
+  if (gemm_y) TARFA_CUDA(launch_k(combine_token_kernel<T, T>, grid, dim3(threads), 0, st, pdl, c));
+  else TARFA_CUDA(launch_k(combine_token_kernel<T, float>, grid, dim3(threads), 0, st, pdl, c));
   TARFA_CUDA(cudaGetLastError());
   stage_mark(4, st);
   return TARFA_OK;
@@ -545,7 +559,19 @@ int permute_smem_bytes(int nwarps, int E) { return (int)(permute_smem_ints(nwarp
 
 template <typename Idx>
 int launch_permute(const Idx* idx, int T_, int K, int E, bool add_shared, const PermuteOut& o,
-                   unsigned* status, cudaStream_t st) {
+                   int32_t* hist, unsigned* status, cudaStream_t st) {
+  const int R = T_ * K;
+  if (R > 2 * kPermRoutes) {   // many routes: two passes over many blocks
+    const int nblk = perm_blocks(R);
+    const int smem_h = E * (int)sizeof(int);
+    const int smem_s = (2 + kPermThreads / 32) * E * (int)sizeof(int);
+    permute_hist_kernel<Idx><<<nblk, kPermThreads, smem_h, st>>>(idx, T_, K, E, hist, o, status);
+    TARFA_CUDA(cudaGetLastError());
+    permute_scatter_kernel<Idx><<<nblk, kPermThreads, smem_s, st>>>(idx, T_, K, E, add_shared ? 1 : 0,
+                                                                    hist, o);
+    TARFA_CUDA(cudaGetLastError());
+    return TARFA_OK;
+  }
   const int threads = 1024;
   const int smem = permute_smem_bytes(threads / 32, E);
   static bool attr_set[kMaxDevices] = {};
@@ -574,23 +600,36 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
     if (int rc = device_info(&st_ptr, &sms)) return rc;
     const int T_ = (int)s.tokens, H = (int)s.hidden, E = (int)s.experts, K = s.top_k;
     const char* err = nullptr;
+    // split K so that the (tile, K range) work items fill the SMs about twice;
+    // shorter fp32 accumulations also narrow the fix-up window (fixup_rel)
+    const int64_t tiles = ((T_ + 127) / 128) * ((E + 255) / 256);
+    const int ksplit = (int)std::max<int64_t>(
+        1, std::min<int64_t>({(int64_t)kRouterMaxSplit, H / 64, 2 * sms / std::max<int64_t>(1, tiles)}));
     if (router_logits_sm100(s.dtype == TARFA_BF16, hidden, T_, H, w_r, E, at<int32_t>(ws, L.units),
-                            at<float>(ws, L.logits), status, sms, st, &err))
+                            at<float>(ws, L.lgpart), ksplit, status, sms, st, &err))
       return fail(TARFA_ERR_CUDA, "%s", err ? err : "router logits");
     row_norms_kernel<T><<<(E + 7) / 8, 256, 0, st>>>(static_cast<const T*>(w_r), E, H,
                                                      at<float>(ws, L.wnorm));
+    // settle the logits the window decides, recompute the rest exactly (one warp
+    // per listed logit, load-balanced), then top-k
     const int grid = (T_ + 7) / 8;
-    topk_fixup_kernel<T><<<grid, 256, 0, st>>>(
-        at<float>(ws, L.logits), static_cast<const T*>(hidden), static_cast<const T*>(w_r),
-        static_cast<const T*>(bias), static_cast<const T*>(w_sg), at<float>(ws, L.wnorm), T_, H, E,
-        K, at<float>(ws, L.logits),
-        at<float>(ws, L.gate_logit), at<int32_t>(ws, L.idx32), at<float>(ws, L.topw), idx_out, w_out,
-        logits_out);
+    unsigned* cnt = at<unsigned>(ws, L.fxcnt);
+    const T* hT = static_cast<const T*>(hidden);
+    const T* bT = static_cast<const T*>(bias);
+    fixup_window_kernel<T><<<grid, 256, 0, st>>>(
+        at<float>(ws, L.lgpart), ksplit, (int64_t)T_ * E, hT, bT, at<float>(ws, L.wnorm),
+        w_sg != nullptr, T_, H, E, at<float>(ws, L.logits), logits_out, at<int32_t>(ws, L.fxlist), cnt);
+    fixup_exact_kernel<T><<<sms * 8, 256, 0, st>>>(
+        hT, static_cast<const T*>(w_r), static_cast<const T*>(w_sg), bT, H, E,
+        at<int32_t>(ws, L.fxlist), cnt, at<float>(ws, L.logits), logits_out, at<float>(ws, L.gate_logit));
+    topk_kernel<T><<<grid, 256, 0, st>>>(at<float>(ws, L.logits), T_, E, K, at<int32_t>(ws, L.idx32),
+                                         at<float>(ws, L.topw), idx_out, w_out, cnt);
     TARFA_CUDA(cudaGetLastError());
     if (!permute) return TARFA_OK;
     PermuteOut o{nullptr, at<int32_t>(ws, L.perm_tok), at<int32_t>(ws, L.perm_slot),
                  at<int32_t>(ws, L.route_row), at<int32_t>(ws, L.units), nullptr};
-    return launch_permute<int32_t>(at<int32_t>(ws, L.idx32), T_, K, E, add_shared, o, status, st);
+    return launch_permute<int32_t>(at<int32_t>(ws, L.idx32), T_, K, E, add_shared, o,
+                                   at<int32_t>(ws, L.phist), status, st);
   }
   RouterArgs a{};
   a.h = hidden;
@@ -791,7 +830,8 @@ int tarfa_b200_permute(const tarfa_moe_shape* shape, const int64_t* top_idx,
   if (int rc = device_info(&status, &sms)) return rc;
   PermuteOut o{seg_offsets, perm_token, perm_slot, nullptr, at<int32_t>(workspace, L.units), nullptr};
   return launch_permute<int64_t>(top_idx, (int)shape->tokens, shape->top_k, (int)shape->experts,
-                                 false, o, status, static_cast<cudaStream_t>(stream));
+                                 false, o, at<int32_t>(workspace, L.phist), status,
+                                 static_cast<cudaStream_t>(stream));
 }
 
 int tarfa_b200_router_topk(const tarfa_moe_shape* shape, const void* hidden,
@@ -826,7 +866,7 @@ int tarfa_b200_experts_forward(const tarfa_moe_shape* shape, const void* hidden,
   if (int rc = check_weights(shape, weights)) return rc;
   if (shape->tokens == 0) return TARFA_OK;
   TARFA_CHECK(hidden && top_idx && top_w && out, "null argument");
-  TARFA_CHECK(aligned16(hidden), "hidden not 16-byte aligned");
+  TARFA_CHECK(aligned16(hidden) && aligned16(out), "hidden / out not 16-byte aligned");
   const Ws L = layout(*shape, TARFA_OP_EXPERTS);
   if (workspace_bytes < L.total || !workspace)
     return fail(TARFA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, L.total);
@@ -839,7 +879,9 @@ int tarfa_b200_experts_forward(const tarfa_moe_shape* shape, const void* hidden,
                at<int32_t>(workspace, L.route_row), at<int32_t>(workspace, L.units),
                at<int32_t>(workspace, L.idx32)};
   stage_mark(0, st);
-  if (int rc = launch_permute<int64_t>(top_idx, T_, K, E, false, o, status, st)) return rc;
+  if (int rc = launch_permute<int64_t>(top_idx, T_, K, E, false, o, at<int32_t>(workspace, L.phist),
+                                      status, st))
+    return rc;
   stage_mark(1, st);
   const bool int4 = weights->kind == TARFA_W_INT4;
   int rc;
@@ -862,7 +904,8 @@ int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
   if (int rc = check_weights(shape, weights)) return rc;
   if (shape->tokens == 0) return TARFA_OK;
   TARFA_CHECK(hidden && router_weight && out, "null argument");
-  TARFA_CHECK(aligned16(hidden) && aligned16(router_weight), "operands not 16-byte aligned");
+  TARFA_CHECK(aligned16(hidden) && aligned16(router_weight) && aligned16(out),
+              "operands not 16-byte aligned");
   TARFA_CHECK(shape->top_k <= shape->experts, "top_k > experts");
   const bool has_shared = shared && shape->shared_inter > 0;
   if (has_shared) {

@@ -144,6 +144,14 @@ template <typename T> TARFA_DEVI uint32_t nib_pair(uint32_t w, int s) {
 constexpr unsigned kStatusBadExpert = 1u;    // TARFA_DEV_BAD_EXPERT_ID
 constexpr unsigned kStatusWaitTimeout = 2u;  // TARFA_DEV_WAIT_TIMEOUT
 
+// kModeExact: dense weights, the exact path's rounding points
+//   (fused_int4.py:191-194 and 240-244).
+// kModeInt4Fused: int4, the fused decode kernel's arithmetic
+//   (moe_kernel.py:27-104: scale folded after the dot, fp32 intermediates).
+// kModeInt4Dequant: int4 dequantised to the model dtype, then the exact path
+//   (fused_int4.py:254-260 with channel_q4.py:10-14).
+enum GemvMode { kModeExact = 0, kModeInt4Fused = 1, kModeInt4Dequant = 2 };
+
 // Programmatic dependent launch.  launch_dependents lets the next kernel of the
 // stream (launched with programmatic stream serialization) be scheduled before
 // this one ends; grid_dep_wait blocks until the previous kernel has completed

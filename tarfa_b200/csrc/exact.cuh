@@ -1,9 +1,9 @@
 // Correctly rounded dot products of model-dtype vectors without fp64 arithmetic.
 //
 // The router's logit is the model-dtype rounding (nearest, ties to even) of
-// the exact dot product h . w_e (the definition the oracle uses).  fp64 vector
-// arithmetic runs at a small fraction of the fp32 rate on this part, so the
-// kernels never accumulate in fp64:
+// the exact dot product h . w_e (the definition the oracle uses).  The kernels
+// accumulate in fp32 only (an fp64 accumulation costs a conversion and an add
+// per product, and measured twice as slow in the 16-token decode router):
 //
 // fast path   Products of two bf16 / fp16 values are exact in fp32 (at most
 //             22 significant bits).  They are summed with TwoSum (Knuth), which
@@ -253,18 +253,30 @@ TARFA_DEVI float exact_finish(ExactAcc x0, const ExactAcc& x1, int chains, const
   return v;
 }
 
-// Correctly rounded a . b (H elements, both from memory) by one warp.
+// Correctly rounded a . b (H elements, both from memory) by one warp.  The
+// chunks are loaded four per lane at a time, so a 3072-element dot makes three
+// round trips to memory, not twelve.
 template <typename T>
 TARFA_DEVI float warp_dot_exact(const T* a, const T* b, int H) {
   const int lane = threadIdx.x & 31;
+  const int nch = H / 8;
   ExactAcc x0 = exact_zero(), x1 = exact_zero();
-  int j = 0;
-  for (int ch = lane; ch < H / 8; ch += 32, ++j) {
-    const uint4 av = ld_cached(a + ch * 8), bv = ld_cached(b + ch * 8);
-    if (j & 1) exact_chunk<T>(x1, av, bv);
-    else exact_chunk<T>(x0, av, bv);
+  for (int c0 = lane; c0 < nch; c0 += 4 * 32) {
+    uint4 av[4], bv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int ch = c0 + 32 * i;
+      av[i] = ch < nch ? ld_cached(a + ch * 8) : make_uint4(0, 0, 0, 0);
+      bv[i] = ch < nch ? ld_cached(b + ch * 8) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (c0 + 32 * i >= nch) break;
+      if (i & 1) exact_chunk<T>(x1, av[i], bv[i]);
+      else exact_chunk<T>(x0, av[i], bv[i]);
+    }
   }
-  const int per_lane = (H / 8 + 31) / 32;
+  const int per_lane = (nch + 31) / 32;
   return exact_finish<T>(x0, x1, 8 * ((per_lane + 1) / 2), a, b, H);
 }
 

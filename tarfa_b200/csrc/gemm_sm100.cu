@@ -143,8 +143,12 @@ int run(const PrefillArgs& a, cudaStream_t st, const char** err) {
 bool router_gemm_supported(int64_t H, int64_t E) { return H % 64 == 0 && E % 16 == 0 && E <= 1024; }
 
 int router_logits_sm100(bool bf16, const void* h, int64_t T, int64_t H, const void* w_r, int64_t E,
-                        int32_t* units, float* logits, unsigned* status, int sms, cudaStream_t st,
-                        const char** err) {
+                        int32_t* units, float* logits, int ksplit, unsigned* status, int sms,
+                        cudaStream_t st, const char** err) {
+  if (ksplit < 1 || ksplit > H / sm100::BK) {
+    *err = "router split out of range";
+    return 1;
+  }
   if (!encoder()) {
     *err = "cuTensorMapEncodeTiled is not available from the driver";
     return 1;
@@ -168,8 +172,10 @@ int router_logits_sm100(bool bf16, const void* h, int64_t T, int64_t H, const vo
   p.ldo = E;
   p.status = status;
   p.idesc = sm100::make_idesc(bf16);
+  p.ksplit = ksplit;
+  p.split_stride = T * E;
   const int64_t tiles = ((T + sm100::BM - 1) / sm100::BM) * ((E + sm100::BN - 1) / sm100::BN);
-  const int grid = (int)std::min<int64_t>(sms, tiles);
+  const int grid = (int)std::min<int64_t>(sms, tiles * ksplit);
   return bf16 ? launch_phase<__nv_bfloat16, 2>(mA, mW, mW, mW, p, grid, st, err)
               : launch_phase<__half, 2>(mA, mW, mW, mW, p, grid, st, err);
 }

@@ -55,6 +55,10 @@ struct Params {
   int64_t ldo;
   unsigned* status;
   uint32_t idesc;
+  // phase 2: each output tile is split over ksplit K ranges; split s writes its
+  // fp32 partial to out + s * split_stride (elements).  1 elsewhere.
+  int ksplit;
+  int64_t split_stride;
 };
 
 TARFA_DEVI uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -234,7 +238,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int ntiles = prefix[ntot];
+  const int ksplit = PHASE == 2 ? p.ksplit : 1;
+  const int ntiles = prefix[ntot] * ksplit;   // (tile, K range) work items
 
   if (warp == 0) {
     if (lane == 0) {
@@ -245,7 +250,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       for (int s = 0; s < STAGES; ++s) issued[s] = -1;
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile(t, prefix, ntot, descs, p, nt_r, nt_s);
+        const int sp = t % ksplit;
+        const TileInfo ti = decode_tile(t / ksplit, prefix, ntot, descs, p, nt_r, nt_s);
         const int slot = ti.shared ? 0 : (p.expert_slot ? p.expert_slot[ti.d.expert] : ti.d.expert);
         const int arow = ti.d.row0 + ti.m * BM;
         const CUtensorMap* b0map;
@@ -267,7 +273,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           brow1 = brow0 + 128;
         }
         const int nkb = ti.K / BK;
-        for (int kb = 0; kb < nkb; ++kb) {
+        const int kb0 = sp * nkb / ksplit, kb1 = (sp + 1) * nkb / ksplit;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(smem_u32(&bars->empty[stage]), phase ^ 1u, abort_flag, p.status)) {
             ok = false;
             break;
@@ -295,14 +302,16 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
-        const TileInfo ti = decode_tile(t, prefix, ntot, descs, p, nt_r, nt_s);
+        const int sp = t % ksplit;
+        const TileInfo ti = decode_tile(t / ksplit, prefix, ntot, descs, p, nt_r, nt_s);
         const int acc = it & 1;
         const uint32_t accph = (uint32_t)(it >> 1) & 1u;
         if (!mbar_wait(smem_u32(&bars->tempty[acc]), accph ^ 1u, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * BN);
         const int nkb = ti.K / BK;
-        for (int kb = 0; kb < nkb; ++kb) {
+        const int kb0 = sp * nkb / ksplit, kb1 = (sp + 1) * nkb / ksplit;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(smem_u32(&bars->full[stage]), phase, abort_flag, p.status)) {
             ok = false;
             break;
@@ -311,7 +320,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma(d, sdesc(sa + kk * 32), sdesc(sa + A_BYTES + kk * 32), p.idesc, (kb | kk) != 0);
+            umma(d, sdesc(sa + kk * 32), sdesc(sa + A_BYTES + kk * 32), p.idesc,
+                 (kb != kb0 || kk != 0));
           umma_commit(smem_u32(&bars->empty[stage]));
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -331,7 +341,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const uint32_t accph = (uint32_t)(it >> 1) & 1u;
       if (!mbar_wait(smem_u32(&bars->tfull[acc]), accph, abort_flag, p.status)) break;
       tc_fence_after();
-      const TileInfo ti = decode_tile(t, prefix, ntot, descs, p, nt_r, nt_s);
+      const int sp = t % ksplit;
+      const TileInfo ti = decode_tile(t / ksplit, prefix, ntot, descs, p, nt_r, nt_s);
       const int rl = ti.m * BM + q * 32 + lane;
       const bool valid = rl < ti.d.nrows;
       const int64_t orow = ti.d.row0 + rl;
@@ -373,7 +384,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           tmem_wait_ld();
           const int col0 = ti.n * BN + j0;
           if (valid && col0 < p.N_s) {
-            float* dst = static_cast<float*>(p.out) + orow * p.ldo + col0;
+            float* dst = static_cast<float*>(p.out) + sp * p.split_stride + orow * p.ldo + col0;
             if (col0 + 16 <= p.N_s) {
               float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll

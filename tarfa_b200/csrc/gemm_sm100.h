@@ -28,11 +28,13 @@ struct PrefillArgs {
 };
 
 // Router logits h . W_r^T in fp32 on the tensor cores (rounding fixed up by
-// the top-k kernel).  units: 8 ints of scratch for a one-unit table.
+// the top-k kernel).  units: 8 ints of scratch for a one-unit table.  The K
+// range is split ksplit ways (1 <= ksplit <= H / 64); split s writes its fp32
+// partial [T, E] at logits + s * T * E.
 bool router_gemm_supported(int64_t H, int64_t E);
 int router_logits_sm100(bool bf16, const void* h, int64_t T, int64_t H, const void* w_r, int64_t E,
-                        int32_t* units, float* logits, unsigned* status, int sms, cudaStream_t st,
-                        const char** err);
+                        int32_t* units, float* logits, int ksplit, unsigned* status, int sms,
+                        cudaStream_t st, const char** err);
 
 // True when the tcgen05 path covers this layer shape (dense experts only).
 bool prefill_supported(int64_t H, int64_t I, int64_t Is, bool dense);

@@ -26,17 +26,12 @@
 #pragma once
 #include "common.cuh"
 #include "routing.cuh"
+#include "combine.cuh"
 
 namespace tarfa {
 
 enum GemvPhase { kGateUp = 0, kDown = 1 };
-// kModeExact: dense weights, the exact path's rounding points
-//   (fused_int4.py:191-194 and 240-244).
-// kModeInt4Fused: int4, the fused decode kernel's arithmetic
-//   (moe_kernel.py:27-104: scale folded after the dot, fp32 intermediates).
-// kModeInt4Dequant: int4 dequantised to the model dtype, then the exact path
-//   (fused_int4.py:254-260 with channel_q4.py:10-14).
-enum GemvMode { kModeExact = 0, kModeInt4Fused = 1, kModeInt4Dequant = 2 };
+
 
 struct GemvArgs {
   const void* x;             // GATE_UP: hidden [T, ld_x]; DOWN: act [R, ld_x]

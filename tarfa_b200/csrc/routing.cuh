@@ -128,6 +128,152 @@ __device__ void block_permute(const Idx* idx, int T, int K, int E, bool add_shar
     }
 }
 
+// ---------------------------------------------------------------------------
+// multi-block permute for large batches: the same outputs as block_permute
+// ---------------------------------------------------------------------------
+// Pass 1: block b counts the experts of routes [b*kPermRoutes, (b+1)*kPermRoutes)
+// into hist[b][E].  Pass 2: every block derives, per expert, the start of its
+// segment (sum of the totals of smaller ids) plus the routes of that expert in
+// earlier blocks, then scatters its routes with stable ranks inside the block
+// (per-warp counts, match_any); block 0 also writes the unit table.
+constexpr int kPermThreads = 256;
+constexpr int kPermRoutes = 2048;
+
+__host__ __device__ inline int perm_blocks(int R) { return (R + kPermRoutes - 1) / kPermRoutes; }
+
+template <typename Idx>
+__global__ void __launch_bounds__(kPermThreads) permute_hist_kernel(const Idx* idx, int T, int K, int E,
+                                                                    int32_t* hist, PermuteOut o,
+                                                                    unsigned* status) {
+  extern __shared__ int sh_hist[];
+  for (int i = threadIdx.x; i < E; i += blockDim.x) sh_hist[i] = 0;
+  __syncthreads();
+  const int R = T * K;
+  const int r0 = blockIdx.x * kPermRoutes, r1 = min(R, r0 + kPermRoutes);
+  for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    const int t = r % T, k = r / T;
+    const int64_t e = (int64_t)idx[(int64_t)t * K + k];
+    if (e >= 0 && e < E) atomicAdd(&sh_hist[(int)e], 1);
+    else if (e != E) raise_status(status, kStatusBadExpert);
+    if (o.idx32) o.idx32[t * K + k] = (int32_t)e;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < E; i += blockDim.x) hist[(int64_t)blockIdx.x * E + i] = sh_hist[i];
+}
+
+template <typename Idx>
+__global__ void __launch_bounds__(kPermThreads) permute_scatter_kernel(const Idx* idx, int T, int K, int E,
+                                                                       int add_shared,
+                                                                       const int32_t* hist, PermuteOut o) {
+  extern __shared__ int sh_sc[];
+  const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* base = sh_sc;            // [E] first row of expert e's routes in this block
+  int* tot = sh_sc + E;         // [E] routes of expert e in all blocks
+  int* wcnt = sh_sc + 2 * E;    // [nw][E]
+  __shared__ int s_rows;
+  const int R = T * K, nblk = perm_blocks(R);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int t_all = 0, t_pre = 0;
+    for (int b = 0; b < nblk; ++b) {
+      const int c = hist[(int64_t)b * E + e];
+      t_all += c;
+      if (b < (int)blockIdx.x) t_pre += c;
+    }
+    base[e] = t_pre;
+    tot[e] = t_all;
+  }
+  for (int i = threadIdx.x; i < nw * E; i += blockDim.x) wcnt[i] = 0;
+  __syncthreads();
+  UnitDesc* descs = reinterpret_cast<UnitDesc*>(o.units + 4);
+  if (warp == 0) {   // segment starts: exclusive prefix of the totals over expert ids
+    const int per = (E + 31) / 32;
+    const int b0 = min(lane * per, E), b1 = min(b0 + per, E);
+    int s = 0, nz = 0;
+    for (int e = b0; e < b1; ++e) { s += tot[e]; nz += tot[e] > 0; }
+    int ps = s, pnz = nz;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, ps, d);
+      const int y = __shfl_up_sync(0xffffffffu, pnz, d);
+      if (lane >= d) { ps += x; pnz += y; }
+    }
+    int es = ps - s, enz = pnz - nz;
+    const int rows = __shfl_sync(0xffffffffu, ps, 31), nunits = __shfl_sync(0xffffffffu, pnz, 31);
+    const bool pub = blockIdx.x == 0;
+    for (int e = b0; e < b1; ++e) {
+      const int cnt = tot[e];
+      if (pub && cnt > 0) { descs[enz] = UnitDesc{e, es, cnt, 0}; ++enz; }
+      if (pub && o.seg_offsets) o.seg_offsets[e] = es;
+      base[e] += es;
+      es += cnt;
+    }
+    if (lane == 0) {
+      s_rows = rows;
+      if (pub) {
+        if (o.seg_offsets) o.seg_offsets[E] = rows;
+        o.units[0] = nunits;
+        o.units[1] = rows;
+        o.units[2] = add_shared ? 1 : 0;
+        o.units[3] = rows;
+        if (add_shared) descs[nunits] = UnitDesc{E, rows, T, 0};
+      }
+    }
+  }
+  // this block's routes, split contiguously over the warps (stable order)
+  const int rb0 = blockIdx.x * kPermRoutes, rb1 = min(R, rb0 + kPermRoutes);
+  const int span = rb1 - rb0;
+  const int r0 = rb0 + (int)((int64_t)span * warp / nw), r1 = rb0 + (int)((int64_t)span * (warp + 1) / nw);
+  for (int r = r0 + lane; r < r1; r += 32) {
+    const int t = r % T, k = r / T;
+    const int64_t e = (int64_t)idx[(int64_t)t * K + k];
+    if (e >= 0 && e < E) atomicAdd(&wcnt[warp * E + (int)e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {   // per-warp cursors
+    int s = base[e];
+    for (int w = 0; w < nw; ++w) {
+      const int c = wcnt[w * E + e];
+      wcnt[w * E + e] = s;
+      s += c;
+    }
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+  for (int rb = r0; rb < r1; rb += 32) {
+    const int r = rb + lane;
+    const bool in = r < r1;
+    const int t = in ? r % T : 0, k = in ? r / T : 0;
+    const int64_t e64 = in ? (int64_t)idx[(int64_t)t * K + k] : -1;
+    const bool routed = in && e64 >= 0 && e64 < E;
+    const int e = routed ? (int)e64 : 0;
+    const unsigned peers = __match_any_sync(0xffffffffu, routed ? e : -1 - lane);
+    const int rank = __popc(peers & lt);
+    const int cur = routed ? wcnt[warp * E + e] : 0;
+    __syncwarp();
+    if (routed && rank == 0) wcnt[warp * E + e] = cur + __popc(peers);
+    __syncwarp();
+    if (routed) {
+      const int row = cur + rank;
+      o.perm_tok[row] = t;
+      if (o.perm_slot) o.perm_slot[row] = k;
+      if (o.route_row) o.route_row[t * K + k] = row;
+    } else if (in && o.route_row) {
+      o.route_row[t * K + k] = -1;
+    }
+  }
+  if (blockIdx.x == 0) {   // rows past the routed ones
+    __syncthreads();
+    const int rows = s_rows;
+    if (add_shared)
+      for (int t = threadIdx.x; t < T; t += blockDim.x) o.perm_tok[rows + t] = t;
+    if (o.perm_slot)
+      for (int r = rows + threadIdx.x; r < R; r += blockDim.x) {
+        o.perm_slot[r] = -1;
+        if (!add_shared) o.perm_tok[r] = -1;
+      }
+  }
+}
+
 // Orderable 32-bit key of a model-dtype logit and its expert id (E <= 65535):
 // larger logit first, then smaller id; -0 and +0 compare equal.
 template <typename T>
