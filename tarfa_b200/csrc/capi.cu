@@ -68,6 +68,27 @@ std::mutex g_dev_mu;
 unsigned* g_status_ptr[kMaxDevices];
 int g_sm_count[kMaxDevices];
 
+// Device address of a pointer for kernel access: device memory as is, mapped
+// page-locked host memory through its device alias.
+int device_alias(const void* p, const void** out) {
+  cudaPointerAttributes at{};
+  TARFA_CUDA(cudaPointerGetAttributes(&at, p));
+  if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) {
+    *out = p;
+    return TARFA_OK;
+  }
+  if (at.type == cudaMemoryTypeHost && at.devicePointer) {
+    *out = at.devicePointer;
+    return TARFA_OK;
+  }
+  return fail(TARFA_ERR_INVALID, "pointer %p is neither device memory nor mapped page-locked host memory", p);
+}
+
+__global__ void stage_copy_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, size_t n16) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n16) dst[i] = src[i];
+}
+
 int device_info(unsigned** status, int* sms) {
   int dev = 0;
   TARFA_CUDA(cudaGetDevice(&dev));
@@ -775,6 +796,25 @@ size_t tarfa_b200_workspace_size(const tarfa_moe_shape* shape, int32_t op) {
 int tarfa_b200_set_fused_decode_max_tokens(int64_t tokens) {
   if (tokens < 0) return fail(TARFA_ERR_INVALID, "fused_decode_max_tokens %lld < 0", (long long)tokens);
   g_fused_max_tokens.store(tokens);
+  return TARFA_OK;
+}
+
+int tarfa_b200_stage_copy(void* dst, const void* src, size_t bytes, void* stream) {
+  TARFA_CHECK(dst && src, "null pointer");
+  TARFA_CHECK(aligned16(dst) && aligned16(src) && bytes % 16 == 0,
+              "stage_copy needs 16-byte aligned pointers and a multiple of 16 bytes");
+  if (bytes == 0) return TARFA_OK;
+  const void* d = nullptr;
+  const void* sp = nullptr;
+  if (int rc = device_alias(dst, &d)) return rc;
+  if (int rc = device_alias(src, &sp)) return rc;
+  const size_t n16 = bytes / 16;
+  const unsigned threads = 256;
+  const size_t blocks = (n16 + threads - 1) / threads;
+  TARFA_CHECK(blocks <= 0x7fffffffu, "stage_copy of %zu bytes is too large", bytes);
+  stage_copy_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(const_cast<void*>(d)), static_cast<const uint4*>(sp), n16);
+  TARFA_CUDA(cudaGetLastError());
   return TARFA_OK;
 }
 

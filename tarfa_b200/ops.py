@@ -299,14 +299,54 @@ class MoePlan:
         api.check(self._fn(*self._args, C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
         return self.out
 
-    def capture(self) -> torch.cuda.CUDAGraph:
-        """Record the layer into a CUDA graph (after one eager warm-up run)."""
+    def capture(self, host_in: torch.Tensor | None = None,
+                host_out: torch.Tensor | None = None) -> torch.cuda.CUDAGraph:
+        """Record the layer into a CUDA graph (after one eager warm-up run).
+
+        With ``host_in`` / ``host_out`` (pinned host tensors shaped like
+        ``h`` / ``out``) the graph also copies the tokens in from ``host_in``
+        and the result out to ``host_out`` (kernel copies over the host link up
+        to 1 MiB, ``stage_copy``; the copy engine above): a serving step is then
+        one replay, the copies back to back with the kernels, after which the host reads
+        ``host_out`` once the stream (or an event recorded after the replay)
+        has completed.
+        """
+        for t, ref, name in ((host_in, self.h, "host_in"), (host_out, self.out, "host_out")):
+            if t is not None and (t.device.type != "cpu" or not t.is_pinned() or
+                                  t.shape != ref.shape or t.dtype != ref.dtype):
+                raise RuntimeError(f"{name} must be a pinned host tensor shaped like the plan's {name[5:]}")
         self.run()
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
+            if host_in is not None:
+                _host_copy(self.h, host_in)
             self.run()
+            if host_out is not None:
+                _host_copy(host_out, self.out)
         return g
+
+
+_STAGE_COPY_MAX = 1 << 20
+
+
+def stage_copy(dst: torch.Tensor, src: torch.Tensor) -> None:
+    """Kernel copy between device memory and pinned host memory (same shape and
+    dtype, contiguous) on the current stream: for small transfers, faster than
+    the copy engine (``tarfa_b200_stage_copy``)."""
+    if dst.shape != src.shape or dst.dtype != src.dtype or not (dst.is_contiguous() and src.is_contiguous()):
+        raise RuntimeError("stage_copy: dst and src must be contiguous with the same shape and dtype")
+    dev = dst.device if dst.is_cuda else src.device
+    api.check(api.lib().tarfa_b200_stage_copy(_ptr(dst), _ptr(src), dst.numel() * dst.element_size(),
+                                              _stream(dev)))
+
+
+def _host_copy(dst: torch.Tensor, src: torch.Tensor) -> None:
+    nbytes = dst.numel() * dst.element_size()
+    if nbytes <= _STAGE_COPY_MAX and nbytes % 16 == 0:
+        stage_copy(dst, src)
+    else:
+        dst.copy_(src, non_blocking=True)
 
 
 def dequant_int4(packed: torch.Tensor, scale: torch.Tensor, group: int = 0) -> torch.Tensor:
