@@ -289,8 +289,24 @@ int launch_gemv_ntb(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStrea
   return launch_gemv<T, MODE, PHASE, KSPLIT, 2>(a, max_tiles, sms, st, pdl, smem);
 }
 
-constexpr int kKsplitGateUp = 8;
-constexpr int kKsplitDown = 4;
+// Warps sharing one tile's K (the rest of the CTA's warps take other tiles).
+// Measured on the config-1 layer with the A/B harness: gate_up 4 and down 2
+// beat 8 and 4 (T = 1: 53.3 vs 55.1 us per layer; T = 16: 340 vs 369 us).
+constexpr int kKsplitGateUp = 4;
+constexpr int kKsplitDown = 2;
+// int4 tiles hold a quarter of the bytes of dense ones, so fewer warps share a
+// tile's K (the per-tile reduction and epilogue amortise over more data).
+// Measured on the config-1 layer (group 128): gate_up split 4 at 1-2 tokens
+// (51 vs 59 us per layer at T = 1), 2 from 4 tokens (313 vs 363 us at T = 16);
+// down split 2.
+
+template <typename T, int MODE, int PHASE>
+int launch_gemv_q4(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStream_t st, bool pdl,
+                   int smem) {
+  if (PHASE == kGateUp && T_ <= 2)
+    return launch_gemv_ntb<T, MODE, PHASE, 4>(a, max_tiles, T_, sms, st, pdl, smem);
+  return launch_gemv_ntb<T, MODE, PHASE, 2>(a, max_tiles, T_, sms, st, pdl, smem);
+}
 
 // Token count from which dense layers take the tcgen05 grouped-GEMM path
 // (tarfa_b200_set_gemm_min_tokens); below it the tensor-core GEMV path.
@@ -481,10 +497,8 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
   } else {
     g.which = 1;
     rc = mode == kModeInt4Fused
-             ? launch_gemv_ntb<T, kModeInt4Fused, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st,
-                                                                          pdl, smem)
-             : launch_gemv_ntb<T, kModeInt4Dequant, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms,
-                                                                            st, pdl, smem);
+             ? launch_gemv_q4<T, kModeInt4Fused, kGateUp>(g, tiles_gu, T_, sms, st, pdl, smem)
+             : launch_gemv_q4<T, kModeInt4Dequant, kGateUp>(g, tiles_gu, T_, sms, st, pdl, smem);
     if (rc == TARFA_OK && Is) {
       GemvArgs gs = g;
       gs.which = 2;
@@ -526,9 +540,8 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
   } else {
     g.which = 1;
     rc = mode == kModeInt4Fused
-             ? launch_gemv_ntb<T, kModeInt4Fused, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st, pdl)
-             : launch_gemv_ntb<T, kModeInt4Dequant, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st,
-                                                                        pdl);
+             ? launch_gemv_q4<T, kModeInt4Fused, kDown>(g, tiles_dn, T_, sms, st, pdl, 0)
+             : launch_gemv_q4<T, kModeInt4Dequant, kDown>(g, tiles_dn, T_, sms, st, pdl, 0);
     if (rc == TARFA_OK && Is) {
       GemvArgs gs = g;
       gs.which = 2;
