@@ -38,6 +38,15 @@ class SharedExpert(C.Structure):
                 ("gate_weight", C.c_void_p)]
 
 
+EP_MAX_RANKS = 8
+EP_IPC_HANDLE_BYTES = 64
+
+
+class EpGroup(C.Structure):
+    _fields_ = [("world", C.c_int32), ("rank", C.c_int32), ("max_tokens", C.c_int64),
+                ("boxes", C.c_void_p * EP_MAX_RANKS)]
+
+
 # name -> (restype, argtypes); every symbol include/tarfa_b200.h declares
 _P = C.c_void_p
 SIGNATURES = {
@@ -66,6 +75,15 @@ SIGNATURES = {
     "tarfa_b200_set_fused_decode_max_tokens": (C.c_int, [C.c_int64]),
     "tarfa_b200_set_decode_routing_max_tokens": (C.c_int, [C.c_int64]),
     "tarfa_b200_stage_copy": (C.c_int, [_P, _P, C.c_size_t, _P]),
+    "tarfa_b200_ep_box_bytes": (C.c_size_t, [C.POINTER(MoeShape), C.c_int32, C.c_int64]),
+    "tarfa_b200_ep_workspace_size": (C.c_size_t, [C.POINTER(MoeShape), C.c_int32, C.c_int64]),
+    "tarfa_b200_ep_box_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), _P]),
+    "tarfa_b200_ep_box_open": (C.c_int, [_P, C.POINTER(C.c_void_p)]),
+    "tarfa_b200_ep_box_close": (C.c_int, [_P]),
+    "tarfa_b200_ep_box_free": (C.c_int, [_P]),
+    "tarfa_b200_ep_moe_layer": (C.c_int, [C.POINTER(MoeShape), _P, _P, _P, C.POINTER(MoeWeights),
+                                          C.POINTER(SharedExpert), C.POINTER(EpGroup), _P, _P, _P,
+                                          _P, C.c_size_t, _P]),
 }
 
 _lock = threading.Lock()

@@ -19,6 +19,7 @@
 #include "int4.cuh"
 #include "router.cuh"
 #include "decode_fused.cuh"
+#include "ep_p2p.cuh"
 
 using namespace tarfa;
 
@@ -300,12 +301,15 @@ constexpr int kKsplitDown = 2;
 // (51 vs 59 us per layer at T = 1), 2 from 4 tokens (313 vs 363 us at T = 16);
 // down split 2.
 
+// T_: tokens of the batch (picks the K split, which fixes the fp32 summation
+// order); rows: most rows of one unit (picks the token blocks; -1: T_).
 template <typename T, int MODE, int PHASE>
 int launch_gemv_q4(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStream_t st, bool pdl,
-                   int smem) {
+                   int smem, int rows = -1) {
+  if (rows < 0) rows = T_;
   if (PHASE == kGateUp && T_ <= 2)
-    return launch_gemv_ntb<T, MODE, PHASE, 4>(a, max_tiles, T_, sms, st, pdl, smem);
-  return launch_gemv_ntb<T, MODE, PHASE, 2>(a, max_tiles, T_, sms, st, pdl, smem);
+    return launch_gemv_ntb<T, MODE, PHASE, 4>(a, max_tiles, rows, sms, st, pdl, smem);
+  return launch_gemv_ntb<T, MODE, PHASE, 2>(a, max_tiles, rows, sms, st, pdl, smem);
 }
 
 // Token count from which dense layers take the tcgen05 grouped-GEMM path
@@ -795,6 +799,213 @@ int run_decode_layer(const tarfa_moe_shape& s, const void* hidden, const void* w
                         false, out, st, true);
 }
 
+// ===========================================================================
+// expert parallelism over peer memory (ep_p2p.cuh)
+// ===========================================================================
+constexpr size_t kEpCounters = 2112;   // three last-block counters inside the zero header
+static_assert(kEpCounters + 16 <= kZeroHeaderBytes, "EP counters outside the zero header");
+
+struct EpWs {
+  Ws w;
+  size_t local_idx;
+};
+
+// Workspace of one expert-parallel layer, sized for max_tokens (the same
+// offsets serve every batch up to it).
+EpWs ep_layout(const tarfa_moe_shape& s, int N, int64_t Tmax) {
+  const int64_t K = s.top_k, E = s.experts, H = s.hidden;
+  const int64_t e_per = E / N, R = N * Tmax * K;
+  const int64_t Imax = std::max<int64_t>(s.inter, s.shared_inter);
+  const int64_t Umax = std::min<int64_t>(R, e_per) + 1;
+  EpWs L{};
+  size_t o = kZeroHeaderBytes;
+  auto take = [&](size_t b) { size_t at = o; o += align256(b); return at; };
+  L.w.logits = take(Tmax * E * 4);
+  L.w.gate_logit = take(Tmax * 4);
+  L.w.idx32 = take(Tmax * K * 4);
+  L.w.topw = take(Tmax * K * 4);
+  L.w.units = take((4 + 4 * Umax) * 4);
+  L.w.perm_tok = take((R + Tmax) * 4);
+  L.local_idx = take(R * 4);
+  L.w.act = take((R + Tmax) * Imax * 2);
+  L.w.y = take((R + Tmax) * H * 4);
+  L.w.total = o;
+  return L;
+}
+
+int check_ep(const tarfa_moe_shape* s, const tarfa_ep_group* g) {
+  TARFA_CHECK(g, "null ep group");
+  TARFA_CHECK(g->world >= 1 && g->world <= TARFA_EP_MAX_RANKS, "ep world %d not in [1, %d]",
+              g->world, TARFA_EP_MAX_RANKS);
+  TARFA_CHECK(g->rank >= 0 && g->rank < g->world, "ep rank %d of %d", g->rank, g->world);
+  TARFA_CHECK(s->experts % g->world == 0, "%lld experts do not shard over %d ranks",
+              (long long)s->experts, g->world);
+  TARFA_CHECK(g->max_tokens >= 1 && g->max_tokens * s->top_k * g->world <= 8192,
+              "ep max_tokens %lld (max_tokens * top_k * world must be <= 8192)",
+              (long long)g->max_tokens);
+  for (int r = 0; r < g->world; ++r)
+    TARFA_CHECK(g->boxes[r] && aligned16(g->boxes[r]), "ep box %d null or not 16-byte aligned", r);
+  return TARFA_OK;
+}
+
+template <typename T>
+int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, const void* bias,
+                 const tarfa_moe_weights& w, const tarfa_shared_expert* sh, const tarfa_ep_group& grp,
+                 void* out, int64_t* idx_out, float* w_out, const EpWs& L, void* ws,
+                 unsigned* status, int sms, cudaStream_t st) {
+  const int N = grp.world, T_ = (int)s.tokens, K = s.top_k, E = (int)s.experts, H = (int)s.hidden;
+  const int e_per = E / N, S = (int)grp.max_tokens * K, R = N * S;
+  const int I = (int)s.inter, Is = sh ? (int)s.shared_inter : 0;
+  const int Imax = std::max(I, Is);
+  const bool int4 = w.kind == TARFA_W_INT4;
+  const int mode = !int4 ? kModeExact : (T_ == 1 ? kModeInt4Fused : kModeInt4Dequant);
+  // rows an owner can receive: one per token and source for each of its experts
+  const int rows_max = std::min(R, N * T_ * K);
+  const int units_max = std::min(rows_max, e_per);
+  const int rows_unit = N * T_;   // most rows of one unit (token batches of the GEMV)
+
+  stage_mark(0, st);
+  if (int rc = launch_router_logits<T>(s, hidden, w_r, bias, sh ? sh->gate_weight : nullptr, L.w, ws,
+                                       sms, st))
+    return rc;
+  stage_mark(1, st);
+  ep::Args a{};
+  a.T = T_;
+  a.K = K;
+  a.H = H;
+  a.E = E;
+  a.N = N;
+  a.rank = grp.rank;
+  a.S = S;
+  a.e_per = e_per;
+  a.mode = mode;
+  a.has_shared = sh != nullptr;
+  for (int r = 0; r < N; ++r) a.boxes[r] = grp.boxes[r];
+  a.logits = at<float>(ws, L.w.logits);
+  a.h = hidden;
+  a.idx32 = at<int32_t>(ws, L.w.idx32);
+  a.topw = at<float>(ws, L.w.topw);
+  a.idx_out = idx_out;
+  a.w_out = w_out;
+  a.local_idx = at<int32_t>(ws, L.local_idx);
+  a.units = at<int32_t>(ws, L.w.units);
+  a.perm_tok = at<int32_t>(ws, L.w.perm_tok);
+  a.counters = at<unsigned>(ws, kEpCounters);
+  a.y = at<float>(ws, L.w.y);
+  a.gate_logit = at<float>(ws, L.w.gate_logit);
+  a.out = out;
+  a.status = status;
+  // about 32 blocks store the token rows; every block tops-k its own token
+  const int chunks = std::max(1, std::min(8, 32 / T_));
+  const int ex_smem = permute_smem_bytes(ep::kExchangeThreads / 32, e_per);
+  TARFA_CUDA(launch_k(ep::exchange_kernel<T>, dim3(T_, chunks), dim3(ep::kExchangeThreads),
+                      (size_t)ex_smem, st, true, a));
+
+  // ---- local experts over the inbox rows (shared expert on own tokens first)
+  const ep::Box B = ep::box_layout(N, S, H, sizeof(T));
+  GemvArgs g{};
+  g.units = a.units;
+  g.E = e_per;
+  g.expert_slot = w.expert_slot;
+  g.status = status;
+  g.x = static_cast<const char*>(grp.boxes[grp.rank]) + B.x;
+  g.ld_x = H;
+  g.x_sh = hidden;
+  g.perm_tok = a.perm_tok;
+  g.N_r = I;
+  g.K_r = H;
+  g.N_s = Is;
+  g.K_s = H;
+  g.sw0 = sh ? sh->gate_proj : nullptr;
+  g.sw1 = sh ? sh->up_proj : nullptr;
+  g.out = at<void>(ws, L.w.act);
+  g.ld_out = Imax;
+  g.w = w.gate_up;
+  g.route_mode = 3;
+  g.sh_row0 = R;
+  g.route.T = T_;
+  g.route.add_shared = sh != nullptr;
+  if (int4) {
+    g.w_estride = (int64_t)2 * I * H / 8;
+    g.w_rstride = H / 8;
+    g.sc = w.gate_up_scale;
+    g.s_rstride = w.group ? H / w.group : 1;
+    g.s_estride = (int64_t)2 * I * g.s_rstride;
+    g.group = w.group;
+  } else {
+    g.w_estride = (int64_t)2 * I * H;
+    g.w_rstride = H;
+  }
+  int rc;
+  if (!int4) {
+    g.which = 3;
+    rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(
+        g, units_max * (I / 8) + Is / 8, rows_unit, sms, st, true);
+  } else {
+    GemvArgs gs = g;
+    g.which = 1;
+    rc = mode == kModeInt4Fused
+             ? launch_gemv_q4<T, kModeInt4Fused, kGateUp>(g, units_max * (I / 8), T_, sms, st, true, 0, rows_unit)
+             : launch_gemv_q4<T, kModeInt4Dequant, kGateUp>(g, units_max * (I / 8), T_, sms, st, true, 0, rows_unit);
+    if (rc == TARFA_OK && Is) {
+      gs.which = 2;
+      rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(gs, Is / 8, T_, sms, st, true);
+    }
+  }
+  if (rc) return rc;
+  stage_mark(2, st);
+  g.x = at<void>(ws, L.w.act);
+  g.ld_x = Imax;
+  g.x_sh = nullptr;
+  g.perm_tok = nullptr;
+  g.N_r = H;
+  g.K_r = I;
+  g.N_s = H;
+  g.K_s = Is;
+  g.sw0 = sh ? sh->down_proj : nullptr;
+  g.sw1 = nullptr;
+  g.out = at<void>(ws, L.w.y);
+  g.ld_out = H;
+  g.w = w.down;
+  g.route_mode = 0;
+  if (int4) {
+    g.w_estride = (int64_t)H * I / 8;
+    g.w_rstride = I / 8;
+    g.sc = w.down_scale;
+    g.s_rstride = w.group ? I / w.group : 1;
+    g.s_estride = (int64_t)H * g.s_rstride;
+  } else {
+    g.w_estride = (int64_t)H * I;
+    g.w_rstride = I;
+  }
+  if (!int4) {
+    g.which = 3;
+    rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(
+        g, (units_max + (Is ? 1 : 0)) * (H / 16), rows_unit, sms, st, true);
+  } else {
+    g.which = 1;
+    rc = mode == kModeInt4Fused
+             ? launch_gemv_q4<T, kModeInt4Fused, kDown>(g, units_max * (H / 16), T_, sms, st, true, 0, rows_unit)
+             : launch_gemv_q4<T, kModeInt4Dequant, kDown>(g, units_max * (H / 16), T_, sms, st, true, 0, rows_unit);
+    if (rc == TARFA_OK && Is) {
+      GemvArgs gs = g;
+      gs.which = 2;
+      rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(gs, H / 16, T_, sms, st, true);
+    }
+  }
+  if (rc) return rc;
+  stage_mark(3, st);
+
+  // ---- outputs back to their sources, then the combine ----------------------
+  const int64_t work = (int64_t)rows_max * (H / 4);
+  const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>(2 * sms, (work + ep::kReturnThreads - 1) /
+                                                                           ep::kReturnThreads));
+  TARFA_CUDA(launch_k(ep::return_kernel<T>, dim3(rgrid), dim3(ep::kReturnThreads), 0, st, true, a));
+  TARFA_CUDA(launch_k(ep::combine_kernel<T>, dim3((H / 8 + 31) / 32, T_), dim3(32), 0, st, true, a));
+  stage_mark(4, st);
+  return TARFA_OK;
+}
+
 extern "C" {
 
 int tarfa_b200_abi_version(void) { return TARFA_B200_ABI_VERSION; }
@@ -1166,6 +1377,101 @@ int tarfa_b200_quantize_int4(const void* w, int64_t rows, int64_t cols, int32_t 
       static_cast<__nv_bfloat16*>(scale));
   TARFA_CUDA(cudaGetLastError());
   return TARFA_OK;
+}
+
+// ---- expert parallelism over peer memory ------------------------------------
+size_t tarfa_b200_ep_box_bytes(const tarfa_moe_shape* shape, int32_t world, int64_t max_tokens) {
+  if (!shape || world < 1 || max_tokens < 1) return 0;
+  const int S = (int)(max_tokens * shape->top_k);
+  return ep::box_layout(world, S, (int)shape->hidden, 2).total;
+}
+
+size_t tarfa_b200_ep_workspace_size(const tarfa_moe_shape* shape, int32_t world, int64_t max_tokens) {
+  if (!shape || world < 1 || max_tokens < 1) return 0;
+  return ep_layout(*shape, world, max_tokens).w.total;
+}
+
+int tarfa_b200_ep_box_alloc(size_t bytes, void** box, void* ipc_handle) {
+  TARFA_CHECK(box && bytes > 0, "ep_box_alloc: null box or zero bytes");
+  void* p = nullptr;
+  TARFA_CUDA(cudaMalloc(&p, bytes));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess && ipc_handle) {
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e == cudaSuccess) std::memcpy(ipc_handle, &h, sizeof(h));
+  }
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(TARFA_ERR_CUDA, "ep_box_alloc: %s", cudaGetErrorString(e));
+  }
+  *box = p;
+  return TARFA_OK;
+}
+
+int tarfa_b200_ep_box_open(const void* ipc_handle, void** box) {
+  TARFA_CHECK(ipc_handle && box, "ep_box_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  TARFA_CUDA(cudaIpcOpenMemHandle(box, h, cudaIpcMemLazyEnablePeerAccess));
+  return TARFA_OK;
+}
+
+int tarfa_b200_ep_box_close(void* box) {
+  TARFA_CHECK(box, "ep_box_close: null box");
+  TARFA_CUDA(cudaIpcCloseMemHandle(box));
+  return TARFA_OK;
+}
+
+int tarfa_b200_ep_box_free(void* box) {
+  TARFA_CHECK(box, "ep_box_free: null box");
+  TARFA_CUDA(cudaFree(box));
+  return TARFA_OK;
+}
+
+int tarfa_b200_ep_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
+                            const void* router_weight, const void* router_bias,
+                            const tarfa_moe_weights* weights, const tarfa_shared_expert* shared,
+                            const tarfa_ep_group* group, void* out, int64_t* top_idx_out,
+                            float* top_w_out, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (int rc = check_shape(shape)) return rc;
+  if (int rc = check_ep(shape, group)) return rc;
+  tarfa_moe_shape local = *shape;
+  local.experts = shape->experts / group->world;
+  if (int rc = check_weights(&local, weights)) return rc;
+  TARFA_CHECK(shape->tokens >= 1 && shape->tokens <= group->max_tokens,
+              "ep tokens %lld not in [1, max_tokens = %lld]", (long long)shape->tokens,
+              (long long)group->max_tokens);
+  TARFA_CHECK(hidden && router_weight && out, "null argument");
+  TARFA_CHECK(aligned16(hidden) && aligned16(router_weight) && aligned16(out),
+              "operands not 16-byte aligned");
+  TARFA_CHECK(shape->top_k <= shape->experts, "top_k > experts");
+  const bool has_shared = shared && shape->shared_inter > 0;
+  if (has_shared) {
+    TARFA_CHECK(shared->gate_proj && shared->up_proj && shared->down_proj && shared->gate_weight,
+                "null shared-expert weight");
+    TARFA_CHECK(aligned16(shared->gate_proj) && aligned16(shared->up_proj) &&
+                    aligned16(shared->down_proj) && aligned16(shared->gate_weight),
+                "shared-expert weights not 16-byte aligned");
+  }
+  tarfa_moe_shape s = *shape;
+  if (!has_shared) s.shared_inter = 0;
+  const EpWs L = ep_layout(s, group->world, group->max_tokens);
+  if (workspace_bytes < L.w.total || !workspace)
+    return fail(TARFA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, L.w.total);
+  unsigned* status;
+  int sms;
+  if (int rc = device_info(&status, &sms)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const tarfa_shared_expert* sh = has_shared ? shared : nullptr;
+  return s.dtype == TARFA_BF16
+             ? run_ep_layer<__nv_bfloat16>(s, hidden, router_weight, router_bias, *weights, sh,
+                                           *group, out, top_idx_out, top_w_out, L, workspace,
+                                           status, sms, st)
+             : run_ep_layer<__half>(s, hidden, router_weight, router_bias, *weights, sh, *group,
+                                    out, top_idx_out, top_w_out, L, workspace, status, sms, st);
 }
 
 }  // extern "C"

@@ -36,6 +36,7 @@ enum GemvPhase { kGateUp = 0, kDown = 1 };
 struct GemvArgs {
   const void* x;             // GATE_UP: hidden [T, ld_x]; DOWN: act [R, ld_x]
   int64_t ld_x;
+  const void* x_sh;          // GATE_UP, or null: the shared unit's token rows (else x)
   const int32_t* perm_tok;   // GATE_UP: row -> token; DOWN: unused (row = x row)
   const int32_t* units;
   int which;                 // bit 0: routed units, bit 1: shared unit (dense kernels only)
@@ -58,7 +59,10 @@ struct GemvArgs {
   // 1: route in the kernel from route.logits (decode GATE_UP, routing.cuh);
   // 2: shared unit only, at its fixed rows (decode GATE_UP of the dense shared
   //    expert beside int4 routed experts)
+  // 3: shared unit first at rows [sh_row0, sh_row0 + route.T), then the unit
+  //    table of the previous kernel (expert-parallel receive, ep_p2p.cuh)
   int route_mode;
+  int sh_row0;
   DecodeRoute route;
 };
 
@@ -231,7 +235,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
     if (a.route_mode == 2) nu = 0;
   }
   // the shared unit's rows are fixed when the routing is the router's own top-k
-  const UnitDesc fixed_sh{a.E, a.route.T * a.route.K, a.route.T, 0};
+  const UnitDesc fixed_sh{a.E, a.route_mode == 3 ? a.sh_row0 : a.route.T * a.route.K, a.route.T, 0};
   const int tiles_r = a.N_r / TR, tiles_s = a.N_s / TR;
   // shared-expert tiles first: they need no routing, so with in-kernel routing
   // they run while the router kernel is still finishing
@@ -239,10 +243,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
 
   for (int base = blockIdx.x * kGroups;; base += gridDim.x * kGroups) {
     if (nu < 0 && base + kGroups > nt_s) {   // CTA-uniform: first step with a routed tile
-      const RouteSmem m = cta_route<T, (NTB > 1)>(a.route, a.E, gemv_smem, a.status);
-      units = m.units;
-      perm_tok = m.perm_tok;
-      nu = units[0];
+      if (a.route_mode == 3) {
+        grid_dep_wait();
+        nu = units[0];
+      } else {
+        const RouteSmem m = cta_route<T, (NTB > 1)>(a.route, a.E, gemv_smem, a.status);
+        units = m.units;
+        perm_tok = m.perm_tok;
+        nu = units[0];
+      }
     }
     const int nt_r = ((a.which & 1) && nu > 0) ? nu * tiles_r : 0;
     const int ntiles = nt_s + nt_r;
@@ -308,7 +317,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
           const int r = d.row0 + n;
           // shared-unit rows hold the tokens in order (perm_tok[row0 + n] == n)
           const int xr = PHASE == kGateUp ? (shared_unit ? n : perm_tok[r]) : r;
-          xrow[b] = reinterpret_cast<const char*>(static_cast<const T*>(a.x) + (int64_t)xr * a.ld_x);
+          const void* xb = shared_unit && a.x_sh ? a.x_sh : a.x;
+          xrow[b] = reinterpret_cast<const char*>(static_cast<const T*>(xb) + (int64_t)xr * a.ld_x);
         }
       }
 
@@ -383,7 +393,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   }
   // a kernel that never waited still completes only after its predecessor, so
   // that the next kernel's wait covers the whole chain
-  if (a.route_mode == 2) grid_dep_wait();
+  if (a.route_mode >= 2) grid_dep_wait();
 }
 
 }  // namespace tarfa

@@ -22,14 +22,23 @@ steps go through a backend object, so the same exchange logic runs on CPU
 ``gloo`` ranks in tests with an oracle-backed backend.  Exact (dense) experts
 only: the fused int4 decode keeps fp32 expert outputs across the combine, which
 this exchange does not carry.
+
+:class:`PeerExpertParallelMoE` is the B200 path: the same sharding, but the
+dispatch and the return are stores into the peers' HBM from inside the
+library's kernels (``tarfa_b200_ep_moe_layer``; NVLink peer memory mapped with
+CUDA IPC), with sequence-numbered flags and bounded waits instead of
+collectives, so a decode step is six kernels and no NCCL call.  Dense and int4
+experts; every rank brings the same number of tokens per step.
 """
 from __future__ import annotations
 
+import ctypes as C
 import dataclasses
 
 import torch
 import torch.distributed as dist
 
+from . import _capi as api
 from . import ops
 
 
@@ -158,3 +167,105 @@ class ExpertParallelMoE:
         shared_gated = b.shared_expert(h, s.shared)
         out = b.combine_routes(y_routes, idx, w, E, shared_gated)
         return (out, idx, w) if return_routing else out
+
+
+class PeerExpertParallelMoE:
+    """Expert-parallel layer over NVLink peer memory (one process per GPU).
+
+    Same sharding and results as :class:`ExpertParallelMoE` (rank ``g`` owns
+    experts ``[g*E/N, (g+1)*E/N)``, router and shared expert replicated), but a
+    step is one call of ``tarfa_b200_ep_moe_layer``: the kernels store the
+    routed token rows into the owners' boxes and the expert outputs back into
+    the sources' boxes, so no collective runs on the data path.  Construction
+    and :meth:`close` are collective (they exchange the IPC handles and
+    barrier).  Every rank must call :meth:`forward` the same number of times
+    with the same token count; the calls can be captured in a CUDA graph.
+    """
+
+    def __init__(self, shard: EPShard, group=None, max_tokens: int = 16):
+        self.s = shard
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > api.EP_MAX_RANKS:
+            raise ValueError(f"peer-memory EP supports at most {api.EP_MAX_RANKS} ranks")
+        E, K = shard.num_experts, shard.top_k
+        if E % self.world:
+            raise ValueError(f"{E} experts do not shard evenly over {self.world} ranks")
+        w_r = shard.router
+        ops._need_cuda(w_r, shard.bias)
+        H = w_r.shape[1]
+        self.dtype = w_r.dtype
+        E_loc, I = ops._check_weights(shard.experts, H, self.dtype)
+        if E_loc != E // self.world:
+            raise ValueError(f"rank holds {E_loc} experts, expected {E // self.world}")
+        Is = shard.shared.gate_proj.shape[0] if shard.shared is not None else 0
+        self.dims = (H, E, I, Is, K)
+        self.max_tokens = int(max_tokens)
+        self.device = w_r.device
+        L = api.lib()
+        full = ops._shape(self.max_tokens, H, E, I, Is, K, self.dtype)
+        box_bytes = L.tarfa_b200_ep_box_bytes(C.byref(full), self.world, self.max_tokens)
+        ws_bytes = L.tarfa_b200_ep_workspace_size(C.byref(full), self.world, self.max_tokens)
+        self.ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=self.device)
+        self._box = C.c_void_p()
+        handle = (C.c_uint8 * api.EP_IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            api.check(L.tarfa_b200_ep_box_alloc(box_bytes, C.byref(self._box), handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._peers = []
+        boxes = []
+        with torch.cuda.device(self.device):
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    boxes.append(self._box.value)
+                    continue
+                p = C.c_void_p()
+                buf = (C.c_uint8 * api.EP_IPC_HANDLE_BYTES).from_buffer_copy(hb)
+                api.check(L.tarfa_b200_ep_box_open(buf, C.byref(p)))
+                self._peers.append(p)
+                boxes.append(p.value)
+        arr = (C.c_void_p * api.EP_MAX_RANKS)(*boxes)
+        self._group = api.EpGroup(self.world, self.rank, self.max_tokens, arr)
+        self._wc = shard.experts.c_struct()
+        self._sc = shard.shared.c_struct() if shard.shared is not None else None
+        self._fn = L.tarfa_b200_ep_moe_layer
+        dist.barrier(group)   # every box is mapped everywhere before the first store
+
+    def forward(self, h: torch.Tensor, return_routing: bool = False,
+                out: torch.Tensor | None = None):
+        ops._need_cuda(h, out)
+        T, H = h.shape
+        H0, E, I, Is, K = self.dims
+        if H != H0 or h.dtype != self.dtype:
+            raise RuntimeError("hidden states do not match the layer")
+        if not 1 <= T <= self.max_tokens:
+            raise RuntimeError(f"{T} tokens not in [1, max_tokens={self.max_tokens}]")
+        if out is None:
+            out = torch.empty_like(h)
+        idx = torch.empty((T, K), dtype=torch.int64, device=h.device) if return_routing else None
+        wt = torch.empty((T, K), dtype=torch.float32, device=h.device) if return_routing else None
+        shape = ops._shape(T, H, E, I, Is, K, h.dtype)
+        api.check(self._fn(C.byref(shape), ops._ptr(h), ops._ptr(self.s.router), ops._ptr(self.s.bias),
+                           C.byref(self._wc), C.byref(self._sc) if self._sc is not None else None,
+                           C.byref(self._group), ops._ptr(out), ops._ptr(idx), ops._ptr(wt),
+                           ops._ptr(self.ws), self.ws.numel(), ops._stream(h.device)))
+        return (out, idx, wt) if return_routing else out
+
+    __call__ = forward
+
+    def close(self):
+        """Collective: unmap the peers' boxes, then free this rank's own."""
+        if self._box is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        L = api.lib()
+        with torch.cuda.device(self.device):
+            for p in self._peers:
+                api.check(L.tarfa_b200_ep_box_close(p))
+            self._peers = []
+            dist.barrier(self.group)
+            api.check(L.tarfa_b200_ep_box_free(self._box))
+        self._box = None
