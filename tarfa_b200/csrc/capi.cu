@@ -114,7 +114,7 @@ int device_info(unsigned** status, int* sms) {
 // looked up once per device (with that device current) and cached.
 // ---------------------------------------------------------------------------
 constexpr size_t kNoAllocScratchBytes = TARFA_B200_NOALLOC_SCRATCH_BYTES;
-__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 void* g_noalloc_ptr[kMaxDevices];
 
 int noalloc_scratch(void** out) {
