@@ -802,12 +802,12 @@ int run_decode_layer(const tarfa_moe_shape& s, const void* hidden, const void* w
 // ===========================================================================
 // expert parallelism over peer memory (ep_p2p.cuh)
 // ===========================================================================
-constexpr size_t kEpCounters = 2112;   // three last-block counters inside the zero header
+constexpr size_t kEpCounters = 2112;   // the exchange's last-block counter, inside the zero header
 static_assert(kEpCounters + 16 <= kZeroHeaderBytes, "EP counters outside the zero header");
 
 struct EpWs {
   Ws w;
-  size_t local_idx;
+  size_t local_idx, cur_step, xin;
 };
 
 // Workspace of one expert-parallel layer, sized for max_tokens (the same
@@ -827,6 +827,8 @@ EpWs ep_layout(const tarfa_moe_shape& s, int N, int64_t Tmax) {
   L.w.units = take((4 + 4 * Umax) * 4);
   L.w.perm_tok = take((R + Tmax) * 4);
   L.local_idx = take(R * 4);
+  L.cur_step = take(4);
+  L.xin = take(R * H * 2);
   L.w.act = take((R + Tmax) * Imax * 2);
   L.w.y = take((R + Tmax) * H * 4);
   L.w.total = o;
@@ -890,25 +892,29 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
   a.local_idx = at<int32_t>(ws, L.local_idx);
   a.units = at<int32_t>(ws, L.w.units);
   a.perm_tok = at<int32_t>(ws, L.w.perm_tok);
+  a.xin = at<void>(ws, L.xin);
   a.counters = at<unsigned>(ws, kEpCounters);
+  a.cur_step = at<unsigned>(ws, L.cur_step);
   a.y = at<float>(ws, L.w.y);
   a.gate_logit = at<float>(ws, L.w.gate_logit);
   a.out = out;
   a.status = status;
   // about 32 blocks store the token rows; every block tops-k its own token
   const int chunks = std::max(1, std::min(8, 32 / T_));
-  const int ex_smem = permute_smem_bytes(ep::kExchangeThreads / 32, e_per);
+  const int ex_smem = std::max<int>(
+      ep::kExchangeThreads * (int)sizeof(int),   // the unpack's per-item flags
+      R <= ep::kExchangeThreads ? ep::rank_permute_smem_ints(R) * (int)sizeof(int)
+                                : permute_smem_bytes(ep::kExchangeThreads / 32, e_per));
   TARFA_CUDA(launch_k(ep::exchange_kernel<T>, dim3(T_, chunks), dim3(ep::kExchangeThreads),
                       (size_t)ex_smem, st, true, a));
 
   // ---- local experts over the inbox rows (shared expert on own tokens first)
-  const ep::Box B = ep::box_layout(N, S, H, sizeof(T));
   GemvArgs g{};
   g.units = a.units;
   g.E = e_per;
   g.expert_slot = w.expert_slot;
   g.status = status;
-  g.x = static_cast<const char*>(grp.boxes[grp.rank]) + B.x;
+  g.x = a.xin;
   g.ld_x = H;
   g.x_sh = hidden;
   g.perm_tok = a.perm_tok;
@@ -1383,7 +1389,7 @@ int tarfa_b200_quantize_int4(const void* w, int64_t rows, int64_t cols, int32_t 
 size_t tarfa_b200_ep_box_bytes(const tarfa_moe_shape* shape, int32_t world, int64_t max_tokens) {
   if (!shape || world < 1 || max_tokens < 1) return 0;
   const int S = (int)(max_tokens * shape->top_k);
-  return ep::box_layout(world, S, (int)shape->hidden, 2).total;
+  return ep::box_layout(world, S, (int)shape->hidden).total;
 }
 
 size_t tarfa_b200_ep_workspace_size(const tarfa_moe_shape* shape, int32_t world, int64_t max_tokens) {
