@@ -802,8 +802,6 @@ int run_decode_layer(const tarfa_moe_shape& s, const void* hidden, const void* w
 // ===========================================================================
 // expert parallelism over peer memory (ep_p2p.cuh)
 // ===========================================================================
-constexpr size_t kEpCounters = 2112;   // the exchange's last-block counter, inside the zero header
-static_assert(kEpCounters + 16 <= kZeroHeaderBytes, "EP counters outside the zero header");
 
 struct EpWs {
   Ws w;
@@ -893,7 +891,6 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
   a.units = at<int32_t>(ws, L.w.units);
   a.perm_tok = at<int32_t>(ws, L.w.perm_tok);
   a.xin = at<void>(ws, L.xin);
-  a.counters = at<unsigned>(ws, kEpCounters);
   a.cur_step = at<unsigned>(ws, L.cur_step);
   a.y = at<float>(ws, L.w.y);
   a.gate_logit = at<float>(ws, L.w.gate_logit);

@@ -23,12 +23,12 @@
 //            and a metadata word per slot in every owner's block (the local
 //            expert id, -1 elsewhere); then every block unpacks a share of
 //            this rank's inbox into plain rows of the workspace, polling the
-//            tags, and the last block sorts the rows by local expert into the
-//            unit table of the expert GEMVs and advances the step counter
+//            tags, while block 0 reads every slot's metadata and sorts the
+//            rows by local expert into the unit table of the expert GEMVs
 //   experts  gate_up (shared-expert tiles on this rank's own tokens first,
 //            they need no exchange) and down over the unpacked rows (gemv.cuh)
 //   return   every routed row's fp32 output into its source's box (back[r][j],
-//            one value per word)
+//            one value per word); advances this rank's step counter
 //   combine  polls the returned words, then the routing-weighted sum in the
 //            reference's order plus the gated shared expert.
 // Peer memory is only written, with plain stores; every wait is bounded (about
@@ -79,7 +79,6 @@ struct Args {
   int32_t* local_idx;          // [N*S] inbox row -> local expert (e_per = empty slot)
   int32_t* units;              // unit table of the expert GEMVs
   int32_t* perm_tok;           // [N*S] GEMV row -> inbox row
-  unsigned* counters;          // [1] last-block counter, left at zero
   unsigned* cur_step;          // the step in flight (written by the exchange)
   const float* y;              // [N*S + T, H] expert outputs (routed rows, then shared)
   const float* gate_logit;     // [T] shared-expert gate logits (has_shared)
@@ -122,25 +121,6 @@ TARFA_DEVI bool poll_words(const unsigned long long* p, unsigned tag, unsigned l
     ld_words(p, w0, w1);
   }
   return true;
-}
-
-// Is this the grid's last block to get here?  The barrier orders the block's
-// stores before thread 0's fence; the counter is reset by the last block, so
-// the kernel leaves it at zero.
-TARFA_DEVI bool last_block(unsigned* counter, int* s_flag) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned nb = gridDim.x * gridDim.y;
-    const bool last = atomicAdd(counter, 1u) == nb - 1;
-    if (last) {
-      *counter = 0u;
-      __threadfence();
-    }
-    *s_flag = last;
-  }
-  __syncthreads();
-  return *s_flag != 0;
 }
 
 // Sort of the R <= blockDim inbox rows by local expert (ties by row: the order
@@ -207,13 +187,12 @@ __host__ __device__ inline int unpack_chunks(int R, int nblocks, int H) {
 
 // grid (T, C): block (t, c) routes token t and stores column chunk c of its
 // rows; block (t, 0) also writes the token's ids, weights and metadata.  Then
-// all blocks unpack this rank's inbox; the last block sorts it.
+// block 0 sorts this rank's inbox and the others unpack it.
 template <typename T>
 __global__ void __launch_bounds__(kExchangeThreads) exchange_kernel(const Args a) {
   extern __shared__ int ex_smem[];
   __shared__ int32_t s_idx[32];
   __shared__ float s_w[32];
-  __shared__ int s_flag;
   grid_dep_wait();                       // the router kernel's logits
   const Box B = box_layout(a.N, a.S, a.H);
   const unsigned step = read_step(a, B);
@@ -265,22 +244,59 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_kernel(const Args a
   // Every block of this kernel is resident by now: the GEMV may be scheduled
   // (its shared-expert tiles run while the inbox fills).
   grid_dep_launch_dependents();
-  // ---- receive: unpack this rank's inbox (items = slots x column chunks) ----
+  // ---- receive -------------------------------------------------------------
   const int R = a.N * a.S;
   const int nb = gridDim.x * gridDim.y, b = blockIdx.y * gridDim.x + blockIdx.x;
-  const int CH = unpack_chunks(R, nb, a.H);
   const unsigned long long* xw = reinterpret_cast<const unsigned long long*>(box_at(a, a.rank) + B.x);
   const unsigned long long* mw = reinterpret_cast<const unsigned long long*>(box_at(a, a.rank) + B.meta);
   const long long t0 = clock64();
+  if (b == 0) {
+    // block 0 sorts: every slot's metadata word, then the unit table
+    for (int i = threadIdx.x; i < R; i += blockDim.x) {
+      unsigned long long m = ld_word(mw + i);
+      bool ok = true;
+      while (!tagged(m, tag)) {
+        if (clock64() - t0 > kSpinCycles) {
+          raise_status(a.status, kStatusWaitTimeout);
+          ok = false;
+          break;
+        }
+        m = ld_word(mw + i);
+      }
+      const int id = ok ? (int)(unsigned)m : -1;
+      a.local_idx[i] = (id >= 0 && id < a.e_per) ? id : a.e_per;
+    }
+    __syncthreads();
+    if (R <= (int)blockDim.x) {
+      rank_permute(a.local_idx, R, a.e_per, ex_smem, a.units, a.perm_tok);
+    } else {
+      const PermuteOut o{nullptr, a.perm_tok, nullptr, nullptr, a.units, nullptr};
+      block_permute<int32_t>(a.local_idx, R, 1, a.e_per, false, o, ex_smem, a.status);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (a.has_shared) {   // the shared unit: own tokens at rows [R, R + T)
+        const int nu = a.units[0];
+        a.units[2] = 1;
+        a.units[3] = R;
+        reinterpret_cast<UnitDesc*>(a.units + 4)[nu] = UnitDesc{a.e_per, R, a.T, 0};
+      }
+      *a.cur_step = step;   // for the return (which advances the counter) and the combine
+    }
+    if (nb > 1) return;
+    __syncthreads();
+  }
+  // the other blocks (block 0 too when it is alone) unpack the routed rows:
+  // items = slots x column chunks, in rounds of up to blockDim items; every
+  // thread polls one item's metadata, then the block unpacks the round's rows
+  const int ub = nb > 1 ? b - 1 : 0, unb = nb > 1 ? nb - 1 : 1;
+  const int CH = unpack_chunks(R, unb, a.H);
   const int n_items = R * CH;
   const int cwmax = (W + CH - 1) / CH;   // widest column chunk
-  // rounds of up to blockDim items: every thread polls one item's metadata,
-  // then the block unpacks the rows of the round's routed items
-  for (int base = b; base < n_items; base += nb * (int)blockDim.x) {
-    const int cnt = min((int)blockDim.x, (n_items - base + nb - 1) / nb);
+  for (int base = ub; base < n_items; base += unb * (int)blockDim.x) {
+    const int cnt = min((int)blockDim.x, (n_items - base + unb - 1) / unb);
     if ((int)threadIdx.x < cnt) {
-      const int item = base + threadIdx.x * nb;
-      const int slot = item / CH, c = item - slot * CH;
+      const int slot = (base + threadIdx.x * unb) / CH;
       unsigned long long m = ld_word(mw + slot);
       bool ok = true;
       while (!tagged(m, tag)) {
@@ -292,15 +308,13 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_kernel(const Args a
         m = ld_word(mw + slot);
       }
       const int id = ok ? (int)(unsigned)m : -1;
-      const bool routed = id >= 0 && id < a.e_per;
-      ex_smem[threadIdx.x] = routed;
-      if (c == 0) a.local_idx[slot] = routed ? id : a.e_per;
+      ex_smem[threadIdx.x] = id >= 0 && id < a.e_per;
     }
     __syncthreads();
     for (int x = threadIdx.x; x < cnt * cwmax; x += blockDim.x) {
       const int li = x / cwmax, dw = x - li * cwmax;
       if (!ex_smem[li]) continue;
-      const int item = base + li * nb;
+      const int item = base + li * unb;
       const int slot = item / CH, c = item - slot * CH;
       const int w = (int)((int64_t)W * c / CH) + dw;
       if (w >= (int)((int64_t)W * (c + 1) / CH)) continue;
@@ -313,26 +327,6 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_kernel(const Args a
     }
     __syncthreads();   // ex_smem is reused
   }
-  if (!last_block(a.counters, &s_flag)) return;
-  // ---- last block: sort the inbox rows into the unit table -----------------
-  if (R <= (int)blockDim.x) {
-    rank_permute(a.local_idx, R, a.e_per, ex_smem, a.units, a.perm_tok);
-  } else {
-    const PermuteOut o{nullptr, a.perm_tok, nullptr, nullptr, a.units, nullptr};
-    block_permute<int32_t>(a.local_idx, R, 1, a.e_per, false, o, ex_smem, a.status);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    if (a.has_shared) {   // the shared unit: own tokens at rows [R, R + T)
-      const int nu = a.units[0];
-      a.units[2] = 1;
-      a.units[3] = R;
-      reinterpret_cast<UnitDesc*>(a.units + 4)[nu] = UnitDesc{a.e_per, R, a.T, 0};
-    }
-    // every block has read the step: hand it to the return and the combine, advance it
-    *a.cur_step = step;
-    *reinterpret_cast<volatile unsigned*>(box_at(a, a.rank) + B.step) = step + 1;
-  }
 }
 
 // Routed rows' fp32 outputs back to their sources, one value per tagged word.
@@ -341,7 +335,11 @@ template <typename T>
 __global__ void __launch_bounds__(kReturnThreads) return_kernel(const Args a) {
   grid_dep_wait();                       // the down GEMV's outputs
   const Box B = box_layout(a.N, a.S, a.H);
-  const unsigned long long hi = (unsigned long long)(*a.cur_step + 1) << 32;
+  const unsigned step = *a.cur_step;
+  const unsigned long long hi = (unsigned long long)(step + 1) << 32;
+  // every exchange block has read the step by now (the exchange has completed)
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    *reinterpret_cast<volatile unsigned*>(box_at(a, a.rank) + B.step) = step + 1;
   const int rows = a.units[1];
   const int V = a.H / 4;
   const int64_t n = (int64_t)rows * V;
