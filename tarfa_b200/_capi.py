@@ -44,7 +44,7 @@ EP_IPC_HANDLE_BYTES = 64
 
 class EpGroup(C.Structure):
     _fields_ = [("world", C.c_int32), ("rank", C.c_int32), ("max_tokens", C.c_int64),
-                ("boxes", C.c_void_p * EP_MAX_RANKS)]
+                ("tp", C.c_int32), ("reserved", C.c_int32), ("boxes", C.c_void_p * EP_MAX_RANKS)]
 
 
 # name -> (restype, argtypes); every symbol include/tarfa_b200.h declares

@@ -812,9 +812,9 @@ struct EpWs {
 // offsets serve every batch up to it).
 EpWs ep_layout(const tarfa_moe_shape& s, int N, int64_t Tmax) {
   const int64_t K = s.top_k, E = s.experts, H = s.hidden;
-  const int64_t e_per = E / N, R = N * Tmax * K;
+  const int64_t R = N * Tmax * K;
   const int64_t Imax = std::max<int64_t>(s.inter, s.shared_inter);
-  const int64_t Umax = std::min<int64_t>(R, e_per) + 1;
+  const int64_t Umax = std::min<int64_t>(R, E) + 1;   // any split of the experts over the ranks
   EpWs L{};
   size_t o = kZeroHeaderBytes;
   auto take = [&](size_t b) { size_t at = o; o += align256(b); return at; };
@@ -838,8 +838,13 @@ int check_ep(const tarfa_moe_shape* s, const tarfa_ep_group* g) {
   TARFA_CHECK(g->world >= 1 && g->world <= TARFA_EP_MAX_RANKS, "ep world %d not in [1, %d]",
               g->world, TARFA_EP_MAX_RANKS);
   TARFA_CHECK(g->rank >= 0 && g->rank < g->world, "ep rank %d of %d", g->rank, g->world);
-  TARFA_CHECK(s->experts % g->world == 0, "%lld experts do not shard over %d ranks",
+  TARFA_CHECK(g->tp == 1 || (g->tp == 2 && g->world % 2 == 0),
+              "ep tp %d must be 1, or 2 with an even world (%d)", g->tp, g->world);
+  TARFA_CHECK(s->experts % (g->world / g->tp) == 0, "%lld experts do not shard over %d ranks",
               (long long)s->experts, g->world);
+  if (g->tp == 2)
+    TARFA_CHECK(s->inter % 64 == 0, "ep tp 2 needs inter %lld to split into halves of a multiple of 32",
+                (long long)s->inter);
   TARFA_CHECK(g->max_tokens >= 1 && g->max_tokens * s->top_k * g->world <= 8192,
               "ep max_tokens %lld (max_tokens * top_k * world must be <= 8192)",
               (long long)g->max_tokens);
@@ -854,8 +859,9 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
                  void* out, int64_t* idx_out, float* w_out, const EpWs& L, void* ws,
                  unsigned* status, int sms, cudaStream_t st) {
   const int N = grp.world, T_ = (int)s.tokens, K = s.top_k, E = (int)s.experts, H = (int)s.hidden;
-  const int e_per = E / N, S = (int)grp.max_tokens * K, R = N * S;
-  const int I = (int)s.inter, Is = sh ? (int)s.shared_inter : 0;
+  const int P = grp.tp;            // ranks sharing each expert (halves of its intermediate dim)
+  const int e_per = E / (N / P), S = (int)grp.max_tokens * K, R = N * S;
+  const int I = (int)s.inter / P, Is = sh ? (int)s.shared_inter : 0;   // I: this rank's part
   const int Imax = std::max(I, Is);
   const bool int4 = w.kind == TARFA_W_INT4;
   const int mode = !int4 ? kModeExact : (T_ == 1 ? kModeInt4Fused : kModeInt4Dequant);
@@ -878,6 +884,7 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
   a.rank = grp.rank;
   a.S = S;
   a.e_per = e_per;
+  a.tp = P;
   a.mode = mode;
   a.has_shared = sh != nullptr;
   for (int r = 0; r < N; ++r) a.boxes[r] = grp.boxes[r];
@@ -981,18 +988,28 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
     g.w_estride = (int64_t)H * I;
     g.w_rstride = I;
   }
-  if (!int4) {
+  if (!int4 && P == 1) {
     g.which = 3;
     rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(
         g, (units_max + (Is ? 1 : 0)) * (H / 16), rows_unit, sms, st, true);
   } else {
+    // routed experts alone: int4, or the fp32 partial of this rank's half (P = 2:
+    // one warp per tile, the same sum as one K half of the single-GPU GEMV)
     g.which = 1;
-    rc = mode == kModeInt4Fused
-             ? launch_gemv_q4<T, kModeInt4Fused, kDown>(g, units_max * (H / 16), T_, sms, st, true, 0, rows_unit)
-             : launch_gemv_q4<T, kModeInt4Dequant, kDown>(g, units_max * (H / 16), T_, sms, st, true, 0, rows_unit);
+    g.raw_out = P == 2;
+    if (P == 2)
+      rc = !int4 ? launch_gemv_ntb<T, kModeExact, kDown, 1>(g, units_max * (H / 16), rows_unit, sms, st, true)
+           : mode == kModeInt4Fused
+               ? launch_gemv_ntb<T, kModeInt4Fused, kDown, 1>(g, units_max * (H / 16), rows_unit, sms, st, true)
+               : launch_gemv_ntb<T, kModeInt4Dequant, kDown, 1>(g, units_max * (H / 16), rows_unit, sms, st, true);
+    else
+      rc = mode == kModeInt4Fused
+               ? launch_gemv_q4<T, kModeInt4Fused, kDown>(g, units_max * (H / 16), T_, sms, st, true, 0, rows_unit)
+               : launch_gemv_q4<T, kModeInt4Dequant, kDown>(g, units_max * (H / 16), T_, sms, st, true, 0, rows_unit);
     if (rc == TARFA_OK && Is) {
       GemvArgs gs = g;
       gs.which = 2;
+      gs.raw_out = 0;
       rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(gs, H / 16, T_, sms, st, true);
     }
   }
@@ -1004,7 +1021,10 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
   const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>(2 * sms, (work + ep::kReturnThreads - 1) /
                                                                            ep::kReturnThreads));
   TARFA_CUDA(launch_k(ep::return_kernel<T>, dim3(rgrid), dim3(ep::kReturnThreads), 0, st, true, a));
-  TARFA_CUDA(launch_k(ep::combine_kernel<T>, dim3((H / 8 + 31) / 32, T_), dim3(32), 0, st, true, a));
+  if (P == 2)
+    TARFA_CUDA(launch_k(ep::combine_kernel<T, 2>, dim3((H / 8 + 31) / 32, T_), dim3(32), 0, st, true, a));
+  else
+    TARFA_CUDA(launch_k(ep::combine_kernel<T, 1>, dim3((H / 8 + 31) / 32, T_), dim3(32), 0, st, true, a));
   stage_mark(4, st);
   return TARFA_OK;
 }
@@ -1442,8 +1462,11 @@ int tarfa_b200_ep_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
   if (int rc = check_shape(shape)) return rc;
   if (int rc = check_ep(shape, group)) return rc;
   tarfa_moe_shape local = *shape;
-  local.experts = shape->experts / group->world;
+  local.experts = shape->experts / (group->world / group->tp);
+  local.inter = shape->inter / group->tp;
   if (int rc = check_weights(&local, weights)) return rc;
+  if (group->tp == 2 && weights->kind == TARFA_W_INT4)
+    TARFA_CHECK(weights->group > 0, "ep tp 2 with int4 experts needs group scales (group > 0)");
   TARFA_CHECK(shape->tokens >= 1 && shape->tokens <= group->max_tokens,
               "ep tokens %lld not in [1, max_tokens = %lld]", (long long)shape->tokens,
               (long long)group->max_tokens);

@@ -3,9 +3,15 @@
 // from inside this library's kernels (no collective library on the data path).
 //
 // Every rank owns one "box" in its own HBM, mapped into its peers' address
-// spaces with CUDA IPC.  Experts are sharded in contiguous id ranges: rank o
-// owns [o*E/N, (o+1)*E/N).  Slot j = t*K + k of a source block is route k of
-// token t; S = max_tokens*K slots per block.
+// spaces with CUDA IPC.  Experts are sharded in contiguous id ranges over
+// groups of P ranks (P = 1 or 2): group g = o / P owns experts [g*E/G,
+// (g+1)*E/G), G = N/P, and with P = 2 each rank of the pair holds one half of
+// every such expert's intermediate dimension (rank o: half o % 2).  A route
+// goes to every rank of its expert's group; with P = 2 each returns an fp32
+// partial of the down projection and the source adds the two, half 0 first,
+// before the rounding: the same sum the single-GPU down GEMV forms from its two
+// K halves.  Slot j = t*K + k of a source block is route k of token t; S =
+// max_tokens*K slots per block.
 //
 // Tagged words.  Everything that crosses to another GPU is written as 8-byte
 // words (step + 1) << 32 | payload, 16 bytes per store: an aligned 8-byte
@@ -65,7 +71,8 @@ __host__ __device__ inline Box box_layout(int N, int S, int H) {
 }
 
 struct Args {
-  int T, K, H, E, N, rank, S, e_per;
+  int T, K, H, E, N, rank, S, e_per;   // e_per: experts per group of P ranks
+  int tp;                      // P: ranks sharing each expert (1 or 2)
   int mode;                    // GemvMode of the routed experts (combine arithmetic)
   int has_shared;
   void* boxes[kMaxRanks];      // every rank's box in this process's address space
@@ -219,16 +226,20 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_kernel(const Args a
     const int k = i / nw, w = w0 + (i - k * nw);
     const int e = s_idx[k];
     if (e < 0 || e >= a.E) continue;
-    unsigned long long* dst = reinterpret_cast<unsigned long long*>(box_at(a, e / a.e_per) + B.x) +
-                              ((int64_t)a.rank * a.S + t * K + k) * (a.H / 2) + 2 * w;
     const uint2 v = __ldg(src + w);
-    st_words(dst, hi | v.x, hi | v.y);
+    for (int p = 0; p < a.tp; ++p) {   // every rank of the expert's group
+      unsigned long long* dst =
+          reinterpret_cast<unsigned long long*>(box_at(a, (e / a.e_per) * a.tp + p) + B.x) +
+          ((int64_t)a.rank * a.S + t * K + k) * (a.H / 2) + 2 * w;
+      st_words(dst, hi | v.x, hi | v.y);
+    }
   }
   if (blockIdx.y == 0) {   // metadata: the local id in the owner's block, -1 in the others
     for (int i = threadIdx.x; i < a.N * K; i += blockDim.x) {
       const int o = i / K, k = i - o * K;
       const int e = s_idx[k];
-      const int v = (e >= 0 && e < a.E && e / a.e_per == o) ? e - o * a.e_per : -1;
+      const int g = o / a.tp;
+      const int v = (e >= 0 && e < a.E && e / a.e_per == g) ? e - g * a.e_per : -1;
       st_word(reinterpret_cast<unsigned long long*>(box_at(a, o) + B.meta) + a.rank * a.S + t * K + k,
               hi | (unsigned)v);
     }
@@ -363,8 +374,10 @@ TARFA_DEVI void ldcg8(const float* p, float (&v)[8]) {
 }
 
 // grid (column blocks, T), one warp per block: the combine of the single-GPU
-// layer (combine_token_kernel) over the returned words.
-template <typename T>
+// layer (combine_token_kernel) over the returned words.  P = 2: a route's
+// output is the sum of its two halves' fp32 partials (half 0 first), rounded
+// as the single-GPU down GEMV rounds it.
+template <typename T, int P>
 __global__ void __launch_bounds__(32) combine_kernel(const Args a) {
   __shared__ int s_row[32];
   __shared__ float s_w[32];
@@ -384,7 +397,7 @@ __global__ void __launch_bounds__(32) combine_kernel(const Args a) {
     }
     if (lane < K) {
       const bool valid = e >= 0 && e < a.E;
-      s_row[rank] = valid ? (e / a.e_per) * a.S + t * K + lane : -1;
+      s_row[rank] = valid ? (e / a.e_per) * P * a.S + t * K + lane : -1;   // half 0's row
       s_w[rank] = a.topw[t * K + lane];
     }
   }
@@ -402,30 +415,41 @@ __global__ void __launch_bounds__(32) combine_kernel(const Args a) {
     for (int q = 0; q < 8; ++q) acc[q] = 0.f;
     float sv[8];
     if (a.has_shared) ldcg8(shy + h0, sv);   // issued with the routed rows' loads
-    for (int i0 = 0; i0 < K; i0 += 4) {      // 4 routes' words in flight at a time
-      unsigned long long wv[4][8];
+    constexpr int NB = 8 / P;                // routes' words in flight at a time
+    for (int i0 = 0; i0 < K; i0 += NB) {
+      unsigned long long wv[NB][P][8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < NB; ++i) {
         const int r = i0 + i < K ? s_row[i0 + i] : -1;
         if (r >= 0) {
-          const unsigned long long* p = back + (int64_t)r * a.H + h0;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) ld_words(p + 2 * q, wv[i][2 * q], wv[i][2 * q + 1]);
+          for (int p2 = 0; p2 < P; ++p2) {
+            const unsigned long long* p = back + (int64_t)(r + p2 * a.S) * a.H + h0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ld_words(p + 2 * q, wv[i][p2][2 * q], wv[i][p2][2 * q + 1]);
+          }
         }
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < NB; ++i) {
         if (i0 + i >= K) break;
         const int r = s_row[i0 + i];
         if (r < 0) continue;
-        const unsigned long long* p = back + (int64_t)r * a.H + h0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          poll_words(p + 2 * q, tag, wv[i][2 * q], wv[i][2 * q + 1], t0, a.status);
+        for (int p2 = 0; p2 < P; ++p2) {
+          const unsigned long long* p = back + (int64_t)(r + p2 * a.S) * a.H + h0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            poll_words(p + 2 * q, tag, wv[i][p2][2 * q], wv[i][p2][2 * q + 1], t0, a.status);
+        }
         const float wk = s_w[i0 + i];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const float yv = __uint_as_float((unsigned)wv[i][q]);
+          float yv = __uint_as_float((unsigned)wv[i][0][q]);
+          if (P == 2) {
+            yv = __fadd_rn(yv, __uint_as_float((unsigned)wv[i][P - 1][q]));
+            if (a.mode != kModeInt4Fused) yv = rnd<T>(yv);
+          }
           if (a.mode == kModeInt4Fused) acc[q] = __fadd_rn(acc[q], __fmul_rn(yv, wk));
           else if (router_order) acc[q] = rnd<T>(acc[q] + rnd<T>(rnd<T>(wk) * yv));
           else acc[q] = rnd<T>(acc[q] + rnd<T>(__fmul_rn(yv, wk)));

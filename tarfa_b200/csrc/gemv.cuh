@@ -63,6 +63,7 @@ struct GemvArgs {
   //    table of the previous kernel (expert-parallel receive, ep_p2p.cuh)
   int route_mode;
   int sh_row0;
+  int raw_out;               // DOWN: the fp32 dot itself, not rounded (a K part of a split expert)
   DecodeRoute route;
 };
 
@@ -379,7 +380,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
               *o = Elem<T>::from_f(act);
             } else {
               float* o = static_cast<float*>(a.out) + (int64_t)r * a.ld_out + tt * 16 + g;
-              if (MODE == kModeInt4Fused) {
+              if (MODE == kModeInt4Fused || a.raw_out) {
                 o[0] = va;            // moe_kernel.py:101-102: fp32 per-expert output
                 o[8] = vb;
               } else {

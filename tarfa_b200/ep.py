@@ -169,12 +169,43 @@ class ExpertParallelMoE:
         return (out, idx, w) if return_routing else out
 
 
+def shard_experts(full: ops.ExpertWeights, rank: int, world: int, tp: int = 1) -> ops.ExpertWeights:
+    """This rank's part of a layer's experts for :class:`PeerExpertParallelMoE`.
+
+    tp = 1: experts ``[rank*E/N, (rank+1)*E/N)`` whole.  tp = 2: ranks ``2p`` and
+    ``2p+1`` share experts ``[p*2E/N, (p+1)*2E/N)``; rank ``2p+h`` keeps half ``h``
+    of each one's intermediate dimension (gate and up rows ``[h*I/2, (h+1)*I/2)``,
+    the same down columns), as contiguous copies.
+    """
+    E = full.gate_up.shape[0]
+    groups = world // tp
+    e0, e1 = (rank // tp) * (E // groups), (rank // tp + 1) * (E // groups)
+
+    def rows(t, h):   # gate and up rows of half h: t [E, 2I, ...]
+        n = t.shape[1] // 2
+        a = t[e0:e1, h * n // tp:(h + 1) * n // tp]
+        b = t[e0:e1, n + h * n // tp:n + (h + 1) * n // tp]
+        return torch.cat([a, b], dim=1).contiguous()
+
+    def cols(t, h):   # down columns of half h: t [E, H, K']
+        k = t.shape[2]
+        return t[e0:e1, :, h * k // tp:(h + 1) * k // tp].contiguous()
+
+    h = rank % tp
+    if full.kind == "dense":
+        return ops.ExpertWeights(rows(full.gate_up, h), cols(full.down, h))
+    return ops.ExpertWeights(rows(full.gate_up, h), cols(full.down, h), "int4",
+                             rows(full.gate_up_scale, h), cols(full.down_scale, h), full.group)
+
+
 class PeerExpertParallelMoE:
     """Expert-parallel layer over NVLink peer memory (one process per GPU).
 
-    Same sharding and results as :class:`ExpertParallelMoE` (rank ``g`` owns
-    experts ``[g*E/N, (g+1)*E/N)``, router and shared expert replicated), but a
-    step is one call of ``tarfa_b200_ep_moe_layer``: the kernels store the
+    Same results as :class:`ExpertParallelMoE` (router and shared expert
+    replicated; with ``tp=1`` rank ``g`` owns experts ``[g*E/N, (g+1)*E/N)``,
+    with ``tp=2`` pairs of ranks share their experts by halves, which evens out
+    the pairs' load: :func:`shard_experts` cuts a rank's part), but a step is
+    one call of ``tarfa_b200_ep_moe_layer``: the kernels store the
     routed token rows into the owners' boxes and the expert outputs back into
     the sources' boxes, so no collective runs on the data path.  Construction
     and :meth:`close` are collective (they exchange the IPC handles and
@@ -182,7 +213,7 @@ class PeerExpertParallelMoE:
     with the same token count; the calls can be captured in a CUDA graph.
     """
 
-    def __init__(self, shard: EPShard, group=None, max_tokens: int = 16):
+    def __init__(self, shard: EPShard, group=None, max_tokens: int = 16, tp: int = 1):
         self.s = shard
         self.group = group
         self.world = dist.get_world_size(group)
@@ -190,15 +221,20 @@ class PeerExpertParallelMoE:
         if self.world > api.EP_MAX_RANKS:
             raise ValueError(f"peer-memory EP supports at most {api.EP_MAX_RANKS} ranks")
         E, K = shard.num_experts, shard.top_k
-        if E % self.world:
-            raise ValueError(f"{E} experts do not shard evenly over {self.world} ranks")
+        if tp not in (1, 2) or self.world % tp:
+            raise ValueError(f"tp {tp} must be 1, or 2 with an even number of ranks")
+        groups = self.world // tp
+        if E % groups:
+            raise ValueError(f"{E} experts do not shard evenly over {groups} rank groups")
         w_r = shard.router
         ops._need_cuda(w_r, shard.bias)
         H = w_r.shape[1]
         self.dtype = w_r.dtype
-        E_loc, I = ops._check_weights(shard.experts, H, self.dtype)
-        if E_loc != E // self.world:
-            raise ValueError(f"rank holds {E_loc} experts, expected {E // self.world}")
+        E_loc, I_loc = ops._check_weights(shard.experts, H, self.dtype)
+        if E_loc != E // groups:
+            raise ValueError(f"rank holds {E_loc} experts, expected {E // groups}")
+        I = I_loc * tp
+        self.tp = tp
         Is = shard.shared.gate_proj.shape[0] if shard.shared is not None else 0
         self.dims = (H, E, I, Is, K)
         self.max_tokens = int(max_tokens)
@@ -227,7 +263,7 @@ class PeerExpertParallelMoE:
                 self._peers.append(p)
                 boxes.append(p.value)
         arr = (C.c_void_p * api.EP_MAX_RANKS)(*boxes)
-        self._group = api.EpGroup(self.world, self.rank, self.max_tokens, arr)
+        self._group = api.EpGroup(self.world, self.rank, self.max_tokens, tp, 0, arr)
         self._wc = shard.experts.c_struct()
         self._sc = shard.shared.c_struct() if shard.shared is not None else None
         self._fn = L.tarfa_b200_ep_moe_layer

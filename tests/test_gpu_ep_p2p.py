@@ -6,7 +6,9 @@ replayed from a CUDA graph, for dense and int4 experts.  A group whose second
 rank never runs must end both of its waits with TARFA_DEV_WAIT_TIMEOUT (the
 waits are bounded) and leave the device usable.  Two or more GPUs: one
 process per GPU; every rank's output equals the single-GPU layer on the same
-tokens bit for bit, for eager calls, CUDA-graph replays, dense and int4.
+tokens bit for bit, for eager calls, CUDA-graph replays, dense and int4, with
+whole experts per rank (tp=1) and with pairs of ranks sharing experts by halves
+(tp=2, whose two fp32 partials are added in the single-GPU GEMV's order).
 """
 import ctypes as C
 import os
@@ -69,7 +71,7 @@ class _CGroup:
         self.sc = shared.c_struct()
         self.router = router
         arr = (C.c_void_p * api.EP_MAX_RANKS)(*boxes)
-        self.group = api.EpGroup(world, rank, max_tokens, arr)
+        self.group = api.EpGroup(world, rank, max_tokens, 1, 0, arr)
         shape = ops._shape(max_tokens, s.hidden, s.experts, I, s.shared_inter, 8, torch.bfloat16)
         n = self.L.tarfa_b200_ep_workspace_size(C.byref(shape), world, max_tokens)
         self.ws = torch.zeros(n, dtype=torch.uint8, device=router.device)
@@ -190,12 +192,13 @@ def _worker(rank, world, port, errq):
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                                 device_id=dev)
         from tarfa_b200 import ops
-        from tarfa_b200.ep import EPShard, PeerExpertParallelMoE
-        for kind in ("dense", "int4"):
+        from tarfa_b200.ep import EPShard, PeerExpertParallelMoE, shard_experts
+        cases = [(k, tp) for k in ("dense", "int4") for tp in ((1, 2) if world % 2 == 0 else (1,))]
+        for kind, tp in cases:
             s, L, full, shared = _layer(dev, kind)
-            per = s.experts // world
-            mine = _slice(full, rank * per, (rank + 1) * per)
-            ep = PeerExpertParallelMoE(EPShard(L["router"], mine, shared, s.experts), max_tokens=16)
+            mine = shard_experts(full, rank, world, tp)
+            ep = PeerExpertParallelMoE(EPShard(L["router"], mine, shared, s.experts), max_tokens=16,
+                                       tp=tp)
             gen = torch.Generator(device=dev).manual_seed(100 + rank)
             for T in ((1, 3, 16) if kind == "dense" else (1, 4)):
                 h = torch.randn((T, s.hidden), generator=gen, device=dev).to(torch.bfloat16)
@@ -203,8 +206,8 @@ def _worker(rank, world, port, errq):
                 ref, ridx, rw = ops.moe_layer(h, L["router"], full, shared, return_routing=True)
                 torch.cuda.synchronize()
                 assert ops.device_status() == 0, f"rank {rank}: device status set"
-                assert torch.equal(idx, ridx), f"rank {rank} {kind} T={T}: routing differs"
-                assert torch.equal(out, ref), f"rank {rank} {kind} T={T}: output differs"
+                assert torch.equal(idx, ridx), f"rank {rank} {kind} tp={tp} T={T}: routing differs"
+                assert torch.equal(out, ref), f"rank {rank} {kind} tp={tp} T={T}: output differs"
             static_h = torch.randn((1, s.hidden), generator=gen, device=dev).to(torch.bfloat16)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
@@ -214,7 +217,7 @@ def _worker(rank, world, port, errq):
                 g.replay()
                 ref = ops.moe_layer(static_h, L["router"], full, shared)
                 torch.cuda.synchronize()
-                assert torch.equal(static_out, ref), f"rank {rank} {kind}: graph replay differs"
+                assert torch.equal(static_out, ref), f"rank {rank} {kind} tp={tp}: graph replay differs"
             del g
             assert ops.device_status() == 0
             ep.close()
