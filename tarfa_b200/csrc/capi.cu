@@ -903,8 +903,8 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
   a.gate_logit = at<float>(ws, L.w.gate_logit);
   a.out = out;
   a.status = status;
-  // about 32 blocks store the token rows; every block tops-k its own token
-  const int chunks = std::max(1, std::min(8, 32 / T_));
+  // 32-64 blocks store the token rows and unpack the inbox; every block tops-k its own token
+  const int chunks = std::max(1, std::min(32, 64 / T_));
   const int ex_smem = std::max<int>(
       ep::kExchangeThreads * (int)sizeof(int),   // the unpack's per-item flags
       R <= ep::kExchangeThreads ? ep::rank_permute_smem_ints(R) * (int)sizeof(int)
