@@ -72,7 +72,6 @@ SIGNATURES = {
     "tarfa_b200_shared_expert": (C.c_int, [C.POINTER(MoeShape), _P, C.POINTER(SharedExpert), _P, _P,
                                            C.c_size_t, _P]),
     "tarfa_b200_combine_routes": (C.c_int, [C.POINTER(MoeShape), _P, _P, _P, _P, _P, _P]),
-    "tarfa_b200_set_fused_decode_max_tokens": (C.c_int, [C.c_int64]),
     "tarfa_b200_set_decode_routing_max_tokens": (C.c_int, [C.c_int64]),
     "tarfa_b200_stage_copy": (C.c_int, [_P, _P, C.c_size_t, _P]),
     "tarfa_b200_ep_box_bytes": (C.c_size_t, [C.POINTER(MoeShape), C.c_int32, C.c_int64]),

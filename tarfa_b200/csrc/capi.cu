@@ -18,7 +18,6 @@
 #include "gemv.cuh"
 #include "int4.cuh"
 #include "router.cuh"
-#include "decode_fused.cuh"
 #include "ep_p2p.cuh"
 
 using namespace tarfa;
@@ -245,6 +244,28 @@ int check_weights(const tarfa_moe_shape* s, const tarfa_moe_weights* w) {
   return TARFA_OK;
 }
 
+// Every argument check of the layer entry points, before anything is launched
+// or written.
+int check_layer_args(const tarfa_moe_shape* shape, const void* hidden, const void* router_weight,
+                     const tarfa_moe_weights* weights, const tarfa_shared_expert* shared,
+                     const void* out) {
+  if (int rc = check_shape(shape)) return rc;
+  if (int rc = check_weights(shape, weights)) return rc;
+  if (shape->tokens == 0) return TARFA_OK;
+  TARFA_CHECK(hidden && router_weight && out, "null argument");
+  TARFA_CHECK(aligned16(hidden) && aligned16(router_weight) && aligned16(out),
+              "operands not 16-byte aligned");
+  TARFA_CHECK(shape->top_k <= shape->experts, "top_k > experts");
+  if (shared && shape->shared_inter > 0) {
+    TARFA_CHECK(shared->gate_proj && shared->up_proj && shared->down_proj && shared->gate_weight,
+                "null shared-expert weight");
+    TARFA_CHECK(aligned16(shared->gate_proj) && aligned16(shared->up_proj) &&
+                    aligned16(shared->down_proj) && aligned16(shared->gate_weight),
+                "shared-expert weights not 16-byte aligned");
+  }
+  return TARFA_OK;
+}
+
 // ---------------------------------------------------------------------------
 // launches
 // ---------------------------------------------------------------------------
@@ -254,6 +275,11 @@ int check_weights(const tarfa_moe_shape* s, const tarfa_moe_weights* w) {
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                      bool pdl, Args&&... args) {
+  if (smem > 48 * 1024) {   // above the default dynamic shared-memory limit
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
   if (!pdl) {
     kern<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
     return cudaGetLastError();
@@ -321,100 +347,12 @@ bool use_gemm(const tarfa_moe_shape& s, const tarfa_moe_weights& w, int64_t Is) 
          prefill_supported(s.hidden, s.inter, Is, true);
 }
 
-// Largest batch that takes the fused single-launch decode kernel (0: never).
-// Off by default: measured slower than the multi-kernel sequence so far.
-std::atomic<int64_t> g_fused_max_tokens{0};
-
-bool use_fused_decode(const tarfa_moe_shape& s, const tarfa_moe_weights& w) {
-  return s.tokens >= 1 && s.tokens <= g_fused_max_tokens.load() && s.tokens <= fused::kMaxT &&
-         s.top_k <= fused::kMaxK && !use_gemm(s, w, s.shared_inter) && s.hidden % 16 == 0 &&
-         s.hidden <= 4096;
-}
-
 template <typename T>
-int launch_fused(const tarfa_moe_shape& s, const void* hidden, const void* w_r, const void* bias,
-                 const tarfa_moe_weights& w, const tarfa_shared_expert* sh, void* out,
-                 int64_t* idx_out, float* w_out, const Ws& L, void* ws, unsigned* status, int sms,
-                 cudaStream_t st) {
-  fused::Args a{};
-  a.T = (int)s.tokens;
-  a.H = (int)s.hidden;
-  a.E = (int)s.experts;
-  a.K = s.top_k;
-  a.I = (int)s.inter;
-  a.Is = sh ? (int)s.shared_inter : 0;
-  a.Imax = a.I > a.Is ? a.I : a.Is;
-  a.group = w.group;
-  a.h = hidden;
-  a.w_r = w_r;
-  a.bias = bias;
-  a.w_sg = sh ? sh->gate_weight : nullptr;
-  a.gate_up = w.gate_up;
-  a.down = w.down;
-  a.gu_scale = w.gate_up_scale;
-  a.dn_scale = w.down_scale;
-  a.expert_slot = w.expert_slot;
-  a.sh_gate = sh ? sh->gate_proj : nullptr;
-  a.sh_up = sh ? sh->up_proj : nullptr;
-  a.sh_down = sh ? sh->down_proj : nullptr;
-  a.out = out;
-  a.idx_out = idx_out;
-  a.w_out = w_out;
-  a.logits = at<float>(ws, L.logits);
-  a.gate_logit = at<float>(ws, L.gate_logit);
-  a.act = at<void>(ws, L.act);
-  a.y = at<float>(ws, L.y);
-  a.bar = at<unsigned>(ws, L.bar);
-  a.hb_cnt = at<unsigned>(ws, L.hb_cnt);
-  a.status = status;
-  const bool int4 = w.kind == TARFA_W_INT4;
-  const int mode = !int4 ? kModeExact : (a.T == 1 ? kModeInt4Fused : kModeInt4Dequant);
-  void (*kern)(const fused::Args);
-  if (a.T <= 8) {
-    kern = mode == kModeExact        ? fused::decode_layer_kernel<T, kModeExact, 1>
-           : mode == kModeInt4Fused ? fused::decode_layer_kernel<T, kModeInt4Fused, 1>
-                                    : fused::decode_layer_kernel<T, kModeInt4Dequant, 1>;
-  } else {
-    kern = mode == kModeExact        ? fused::decode_layer_kernel<T, kModeExact, 2>
-           : mode == kModeInt4Fused ? fused::decode_layer_kernel<T, kModeInt4Fused, 2>
-                                    : fused::decode_layer_kernel<T, kModeInt4Dequant, 2>;
-  }
-  static std::mutex attr_mu;
-  static std::set<std::pair<int, const void*>> attr_done;
-  {
-    int dev = 0;
-    TARFA_CUDA(cudaGetDevice(&dev));
-    std::lock_guard<std::mutex> lk(attr_mu);
-    if (!attr_done.count({dev, (const void*)kern})) {
-      TARFA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)fused::kSmemBytes));
-      attr_done.insert({dev, (const void*)kern});
-    }
-  }
-  int per_sm = 0;
-  TARFA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, fused::kThreads,
-                                                           fused::kSmemBytes));
-  if (per_sm < 1) return fail(TARFA_ERR_UNSUPPORTED, "fused decode kernel does not fit an SM");
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(sms);          // one CTA per SM, all co-resident (cooperative)
-  cfg.blockDim = dim3(fused::kThreads);
-  cfg.dynamicSmemBytes = fused::kSmemBytes;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  TARFA_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
-  return TARFA_OK;
-}
-
-template <typename T>
-// dr: in-kernel routing of a decode batch (the gate_up GEMV routes from the
-// router kernel's logits; every launch is a programmatic dependent).
+// chained: the decode chain (run_decode_layer), every launch a programmatic
+// dependent of the previous one.
 int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_weights& w,
                 const tarfa_shared_expert* sh, const Ws& L, void* ws, void* out,
-                unsigned* status, int sms, cudaStream_t st, const DecodeRoute* dr = nullptr) {
+                unsigned* status, int sms, cudaStream_t st, bool chained = false) {
   const int T_ = (int)s.tokens, K = s.top_k, E = (int)s.experts, H = (int)s.hidden;
   const int I = (int)s.inter, Is = sh ? (int)s.shared_inter : 0;
   const int Imax = I > Is ? I : Is;
@@ -487,12 +425,15 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
     g.w_rstride = H;
   }
   const int tiles_gu = Umax * (I / 8) + (Is ? Is / 8 : 0);
-  const bool pdl = dr != nullptr;
-  int smem = 0;
-  if (dr) {
-    g.route_mode = 1;
-    g.route = *dr;
-    smem = route_smem_ints(T_, K, E, kGemvWarps) * (int)sizeof(int);
+  // chained: programmatic dependents of the router kernel, whose last CTA
+  // writes the unit table; the shared expert's tiles stream meanwhile
+  const bool pdl = chained;
+  const int smem = 0;
+  if (chained) {
+    g.route_mode = 3;
+    g.sh_row0 = R;
+    g.sh_rows = T_;
+    g.add_shared = sh != nullptr;
   }
   int rc;
   if (!int4) {
@@ -506,7 +447,7 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
     if (rc == TARFA_OK && Is) {
       GemvArgs gs = g;
       gs.which = 2;
-      if (dr) gs.route_mode = 2;   // fixed shared rows; the routed launch routes
+      if (chained) gs.route_mode = 2;   // fixed shared rows, no unit table needed
       rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(gs, Is / 8, T_, sms, st, pdl);
     }
   }
@@ -660,9 +601,10 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
     fixup_exact_kernel<T><<<sms * 8, 256, 0, st>>>(
         hT, static_cast<const T*>(w_r), static_cast<const T*>(w_sg), bT, H, E,
         at<int32_t>(ws, L.fxlist), cnt, at<float>(ws, L.logits), logits_out, at<float>(ws, L.gate_logit));
-    topk_kernel<T><<<grid, 256, 0, st>>>(at<float>(ws, L.logits), T_, E, K, at<int32_t>(ws, L.idx32),
-                                         at<float>(ws, L.topw), idx_out, w_out, cnt);
-    TARFA_CUDA(cudaGetLastError());
+    TARFA_CUDA(launch_k(topk_kernel<T>, dim3(grid), dim3(256),
+                        (size_t)8 * tie_scratch_ints(E) * sizeof(int), st, false,
+                        at<float>(ws, L.logits), T_, E, K, at<int32_t>(ws, L.idx32),
+                        at<float>(ws, L.topw), idx_out, w_out, cnt));
     if (!permute) return TARFA_OK;
     PermuteOut o{nullptr, at<int32_t>(ws, L.perm_tok), at<int32_t>(ws, L.perm_slot),
                  at<int32_t>(ws, L.route_row), at<int32_t>(ws, L.units), nullptr};
@@ -701,18 +643,18 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
   a.tpw = (int)std::max<int64_t>(1, std::min<int64_t>(a.T, ((int64_t)rows * a.T + target - 1) / target));
   const int64_t items = (int64_t)rows * ((a.T + a.tpw - 1) / a.tpw);
   const int grid = (int)((items + warps - 1) / warps);
-  const int smem = permute_smem_bytes(warps, a.E) +
-                   (a.T * a.K <= kRouterSmemIdx ? a.T * a.K * (int)sizeof(int32_t) : 0);
+  const int smem = (router_tie_offset(a.E, a.T * a.K) + warps * tie_scratch_ints(a.E)) *
+                   (int)sizeof(int);
   const int per_lane = (a.H / 8 + 31) / 32;
 #define TARFA_ROUTER(MC)                                                                  \
-  router_kernel<T, MC><<<grid, kRouterThreads, smem, st>>>(a)
+  TARFA_CUDA(launch_k(router_kernel<T, MC>, dim3(grid), dim3(kRouterThreads), (size_t)smem, st, \
+                      false, a))
   if (per_lane <= 2) TARFA_ROUTER(2);
   else if (per_lane <= 4) TARFA_ROUTER(4);
   else if (per_lane <= 8) TARFA_ROUTER(8);
   else if (per_lane <= 16) TARFA_ROUTER(16);
   else TARFA_ROUTER(32);
 #undef TARFA_ROUTER
-  TARFA_CUDA(cudaGetLastError());
   return TARFA_OK;
 }
 
@@ -721,22 +663,39 @@ int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
 // ===========================================================================
 // exported entry points
 // ===========================================================================
-// Decode batches on the GEMV path route inside the gate_up kernel (routing.cuh):
-// the router kernel only writes logits, and the expert kernels are programmatic
-// dependents of one another.
+// Decode batches on the GEMV path run as one chain of programmatic dependents:
+// the router kernel (its last CTA routes every token), the gate_up GEMV (shared
+// expert first, then the routed tiles once the unit table is there), the down
+// GEMV and the combine.
 std::atomic<int64_t> g_decode_routing_max_tokens{16};
 
 bool use_decode_routing(const tarfa_moe_shape& s, const tarfa_moe_weights& w) {
   return s.tokens <= g_decode_routing_max_tokens.load() && s.tokens <= 16 &&
          s.tokens * s.top_k <= 128 && s.experts <= 1024 &&
-         !use_gemm(s, w, s.shared_inter) && !use_fused_decode(s, w);
+         !use_gemm(s, w, s.shared_inter);
 }
 
 template <typename T>
+// route: the last CTA also runs top-k and permute into the workspace (decode
+// chain); idx_out / w_out receive the routing then.
 int launch_router_logits(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
                          const void* bias, const void* w_sg, const Ws& L, void* ws, int sms,
-                         cudaStream_t st) {
+                         cudaStream_t st, bool route = false, int64_t* idx_out = nullptr,
+                         float* w_out = nullptr, unsigned* status = nullptr) {
   RouterArgs a{};
+  a.route_last = route;
+  if (route) {
+    a.idx32 = at<int32_t>(ws, L.idx32);
+    a.topw = at<float>(ws, L.topw);
+    a.idx_out = idx_out;
+    a.w_out = w_out;
+    a.counter = at<unsigned>(ws, L.counter);
+    a.do_permute = 1;
+    a.add_shared = w_sg != nullptr;
+    a.perm = PermuteOut{nullptr, at<int32_t>(ws, L.perm_tok), at<int32_t>(ws, L.perm_slot),
+                        at<int32_t>(ws, L.route_row), at<int32_t>(ws, L.units), nullptr};
+    a.status = status;
+  }
   a.h = hidden;
   a.w_r = w_r;
   a.bias = bias;
@@ -761,14 +720,17 @@ int launch_router_logits(const tarfa_moe_shape& s, const void* hidden, const voi
   const int64_t items = (int64_t)rows * ((a.T + a.tpw - 1) / a.tpw);
   const int grid = (int)((items + slots - 1) / slots);
   const int per_lane = ((a.H / 8 + a.wpr - 1) / a.wpr + 31) / 32;
-#define TARFA_ROUTER_LOGITS(MC) router_logits_kernel<T, MC><<<grid, kRouterThreads, 0, st>>>(a)
+  const size_t smem =
+      route ? (size_t)(router_tie_offset(a.E, a.T * a.K) + warps * tie_scratch_ints(a.E)) * sizeof(int) : 0;
+#define TARFA_ROUTER_LOGITS(MC)                                                              \
+  TARFA_CUDA(launch_k(router_logits_kernel<T, MC>, dim3(grid), dim3(kRouterThreads), smem, st, \
+                      false, a))
   if (per_lane <= 2) TARFA_ROUTER_LOGITS(2);
   else if (per_lane <= 4) TARFA_ROUTER_LOGITS(4);
   else if (per_lane <= 8) TARFA_ROUTER_LOGITS(8);
   else if (per_lane <= 16) TARFA_ROUTER_LOGITS(16);
   else TARFA_ROUTER_LOGITS(32);
 #undef TARFA_ROUTER_LOGITS
-  TARFA_CUDA(cudaGetLastError());
   return TARFA_OK;
 }
 
@@ -778,23 +740,10 @@ int run_decode_layer(const tarfa_moe_shape& s, const void* hidden, const void* w
                      void* out, int64_t* idx_out, float* w_out, const Ws& L, void* ws,
                      unsigned* status, int sms, cudaStream_t st) {
   if (int rc = launch_router_logits<T>(s, hidden, w_r, bias, sh ? sh->gate_weight : nullptr, L, ws,
-                                       sms, st))
+                                       sms, st, true, idx_out, w_out, status))
     return rc;
   stage_mark(1, st);
-  DecodeRoute dr{};
-  dr.logits = at<float>(ws, L.logits);
-  dr.T = (int)s.tokens;
-  dr.K = s.top_k;
-  dr.add_shared = sh != nullptr;
-  dr.g_units = at<int32_t>(ws, L.units);
-  dr.g_perm_tok = at<int32_t>(ws, L.perm_tok);
-  dr.g_perm_slot = at<int32_t>(ws, L.perm_slot);
-  dr.g_route_row = at<int32_t>(ws, L.route_row);
-  dr.g_idx32 = at<int32_t>(ws, L.idx32);
-  dr.g_topw = at<float>(ws, L.topw);
-  dr.idx_out = idx_out;
-  dr.w_out = w_out;
-  if (int rc = run_experts<T>(s, hidden, w, sh, L, ws, out, status, sms, st, &dr)) return rc;
+  if (int rc = run_experts<T>(s, hidden, w, sh, L, ws, out, status, sms, st, true)) return rc;
   return run_combine<T>(s, L, ws, at<float>(ws, L.topw), w.kind == TARFA_W_INT4, sh != nullptr,
                         false, out, st, true);
 }
@@ -906,9 +855,10 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
   // 32-64 blocks store the token rows and unpack the inbox; every block tops-k its own token
   const int chunks = std::max(1, std::min(32, 64 / T_));
   const int ex_smem = std::max<int>(
-      ep::kExchangeThreads * (int)sizeof(int),   // the unpack's per-item flags
-      R <= ep::kExchangeThreads ? ep::rank_permute_smem_ints(R) * (int)sizeof(int)
-                                : permute_smem_bytes(ep::kExchangeThreads / 32, e_per));
+      {ep::kExchangeThreads * (int)sizeof(int),   // the unpack's per-item flags
+       R <= ep::kExchangeThreads ? ep::rank_permute_smem_ints(R) * (int)sizeof(int)
+                                 : permute_smem_bytes(ep::kExchangeThreads / 32, e_per),
+       tie_scratch_ints(E) * (int)sizeof(int)});  // warp 0's top-k tie order
   TARFA_CUDA(launch_k(ep::exchange_kernel<T>, dim3(T_, chunks), dim3(ep::kExchangeThreads),
                       (size_t)ex_smem, st, true, a));
 
@@ -933,8 +883,8 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
   g.w = w.gate_up;
   g.route_mode = 3;
   g.sh_row0 = R;
-  g.route.T = T_;
-  g.route.add_shared = sh != nullptr;
+  g.sh_rows = T_;
+  g.add_shared = sh != nullptr;
   if (int4) {
     g.w_estride = (int64_t)2 * I * H / 8;
     g.w_rstride = H / 8;
@@ -1038,12 +988,6 @@ const char* tarfa_b200_last_error(void) { return g_last_error.c_str(); }
 size_t tarfa_b200_workspace_size(const tarfa_moe_shape* shape, int32_t op) {
   if (!shape) return 0;
   return layout(*shape, op).total;
-}
-
-int tarfa_b200_set_fused_decode_max_tokens(int64_t tokens) {
-  if (tokens < 0) return fail(TARFA_ERR_INVALID, "fused_decode_max_tokens %lld < 0", (long long)tokens);
-  g_fused_max_tokens.store(tokens);
-  return TARFA_OK;
 }
 
 int tarfa_b200_stage_copy(void* dst, const void* src, size_t bytes, void* stream) {
@@ -1187,21 +1131,9 @@ int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
                          const tarfa_moe_weights* weights, const tarfa_shared_expert* shared,
                          void* out, int64_t* top_idx_out, float* top_w_out,
                          void* workspace, size_t workspace_bytes, void* stream) {
-  if (int rc = check_shape(shape)) return rc;
-  if (int rc = check_weights(shape, weights)) return rc;
+  if (int rc = check_layer_args(shape, hidden, router_weight, weights, shared, out)) return rc;
   if (shape->tokens == 0) return TARFA_OK;
-  TARFA_CHECK(hidden && router_weight && out, "null argument");
-  TARFA_CHECK(aligned16(hidden) && aligned16(router_weight) && aligned16(out),
-              "operands not 16-byte aligned");
-  TARFA_CHECK(shape->top_k <= shape->experts, "top_k > experts");
   const bool has_shared = shared && shape->shared_inter > 0;
-  if (has_shared) {
-    TARFA_CHECK(shared->gate_proj && shared->up_proj && shared->down_proj && shared->gate_weight,
-                "null shared-expert weight");
-    TARFA_CHECK(aligned16(shared->gate_proj) && aligned16(shared->up_proj) &&
-                    aligned16(shared->down_proj) && aligned16(shared->gate_weight),
-                "shared-expert weights not 16-byte aligned");
-  }
   tarfa_moe_shape s = *shape;
   if (!has_shared) s.shared_inter = 0;
   const Ws L = layout(s, TARFA_OP_MOE_LAYER);
@@ -1215,15 +1147,6 @@ int tarfa_b200_moe_layer(const tarfa_moe_shape* shape, const void* hidden,
   const tarfa_shared_expert* sh = has_shared ? shared : nullptr;
   int rc;
   stage_mark(0, st);
-  if (use_fused_decode(s, *weights)) {   // decode batch: one persistent cooperative launch
-    rc = s.dtype == TARFA_BF16
-             ? launch_fused<__nv_bfloat16>(s, hidden, router_weight, router_bias, *weights, sh, out,
-                                           top_idx_out, top_w_out, L, workspace, status, sms, st)
-             : launch_fused<__half>(s, hidden, router_weight, router_bias, *weights, sh, out,
-                                    top_idx_out, top_w_out, L, workspace, status, sms, st);
-    if (!rc) stage_mark(4, st);
-    return rc;
-  }
   if (use_decode_routing(s, *weights)) {
     return s.dtype == TARFA_BF16
                ? run_decode_layer<__nv_bfloat16>(s, hidden, router_weight, router_bias, *weights,
@@ -1339,7 +1262,9 @@ int tarfa_b200_moe_layer_noalloc(const tarfa_moe_shape* shape, const void* hidde
                                  const tarfa_moe_weights* weights,
                                  const tarfa_shared_expert* shared, void* out,
                                  int64_t* top_idx_out, float* top_w_out, void* stream) {
-  if (int rc = check_shape(shape)) return rc;
+  // a rejected or empty call leaves the shared scratch untouched
+  if (int rc = check_layer_args(shape, hidden, router_weight, weights, shared, out)) return rc;
+  if (shape->tokens == 0) return TARFA_OK;
   tarfa_moe_shape s = *shape;
   if (!(shared && shape->shared_inter > 0)) s.shared_inter = 0;
   const Ws L = layout(s, TARFA_OP_MOE_LAYER);

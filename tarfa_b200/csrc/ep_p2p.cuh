@@ -206,8 +206,9 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_kernel(const Args a
   const unsigned tag = step + 1;
   const unsigned long long hi = (unsigned long long)tag << 32;
   const int t = blockIdx.x, K = a.K;
-  if ((threadIdx.x >> 5) == 0)
-    warp_topk<T>(a.logits + (int64_t)t * a.E, a.E, K, s_idx, s_w, nullptr, nullptr, nullptr);
+  if ((threadIdx.x >> 5) == 0)   // ex_smem is the tie scratch here, reused after the barrier
+    warp_topk<T>(a.logits + (int64_t)t * a.E, a.E, K, s_idx, s_w, nullptr, nullptr, nullptr,
+                 reinterpret_cast<uint32_t*>(ex_smem));
   __syncthreads();
   if (blockIdx.y == 0 && threadIdx.x < K) {
     const int j = t * K + threadIdx.x;

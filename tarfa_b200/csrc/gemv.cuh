@@ -55,16 +55,18 @@ struct GemvArgs {
   void* out;                 // GATE_UP: act (model dtype); DOWN: y (fp32)
   int64_t ld_out;
   unsigned* status;
-  // 0: unit table from `units` (written by an earlier kernel);
-  // 1: route in the kernel from route.logits (decode GATE_UP, routing.cuh);
+  // 0: unit table from `units`, written by an earlier kernel (waited for first);
   // 2: shared unit only, at its fixed rows (decode GATE_UP of the dense shared
   //    expert beside int4 routed experts)
-  // 3: shared unit first at rows [sh_row0, sh_row0 + route.T), then the unit
-  //    table of the previous kernel (expert-parallel receive, ep_p2p.cuh)
+  // 3: shared unit first at its fixed rows, then the unit table the previous
+  //    kernel writes (decode: the router's last CTA; expert-parallel receive,
+  //    ep_p2p.cuh).  The shared tiles need no routing, so they stream while the
+  //    previous kernel finishes.
   int route_mode;
-  int sh_row0;
+  int sh_row0;               // modes 2 / 3: first row and token count of the shared unit
+  int sh_rows;
+  int add_shared;            // modes 2 / 3: the shared unit takes part
   int raw_out;               // DOWN: the fp32 dot itself, not rounded (a K part of a split expert)
-  DecodeRoute route;
 };
 
 constexpr int kGemvThreads = 256;
@@ -216,7 +218,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   constexpr int kGroups = kGemvWarps / KSPLIT;              // tiles per CTA step
   constexpr int TR = PHASE == kGateUp ? 8 : 16;             // tile rows per unit index
   __shared__ float red[kGroups][KSPLIT][NTB * 4][32];
-  extern __shared__ int gemv_smem[];                        // routing (route_mode 1)
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int grp = warp / KSPLIT, kw = warp % KSPLIT;
@@ -224,19 +225,19 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
 
   grid_dep_launch_dependents();
   const int32_t* units = a.units;
-  const int32_t* perm_tok = a.perm_tok;
-  int nu = -1;          // routed units; unknown until routed (route_mode 1)
+  const int32_t* const perm_tok = a.perm_tok;
+  int nu = -1;          // routed units; unknown until the unit table is there (mode 3)
   bool has_sh;
   if (a.route_mode == 0) {
     grid_dep_wait();
     nu = units[0];
     has_sh = units[2] != 0;
   } else {
-    has_sh = a.route.add_shared != 0;
+    has_sh = a.add_shared != 0;
     if (a.route_mode == 2) nu = 0;
   }
   // the shared unit's rows are fixed when the routing is the router's own top-k
-  const UnitDesc fixed_sh{a.E, a.route_mode == 3 ? a.sh_row0 : a.route.T * a.route.K, a.route.T, 0};
+  const UnitDesc fixed_sh{a.E, a.sh_row0, a.sh_rows, 0};
   const int tiles_r = a.N_r / TR, tiles_s = a.N_s / TR;
   // shared-expert tiles first: they need no routing, so with in-kernel routing
   // they run while the router kernel is still finishing
@@ -244,15 +245,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
 
   for (int base = blockIdx.x * kGroups;; base += gridDim.x * kGroups) {
     if (nu < 0 && base + kGroups > nt_s) {   // CTA-uniform: first step with a routed tile
-      if (a.route_mode == 3) {
-        grid_dep_wait();
-        nu = units[0];
-      } else {
-        const RouteSmem m = cta_route<T, (NTB > 1)>(a.route, a.E, gemv_smem, a.status);
-        units = m.units;
-        perm_tok = m.perm_tok;
-        nu = units[0];
-      }
+      grid_dep_wait();
+      nu = units[0];
     }
     const int nt_r = ((a.which & 1) && nu > 0) ? nu * tiles_r : 0;
     const int ntiles = nt_s + nt_r;

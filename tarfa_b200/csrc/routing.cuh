@@ -6,6 +6,7 @@
 // torch.where(one_hot(idx).permute(2,1,0)[e]).
 #pragma once
 #include "common.cuh"
+#include "topk_ties.cuh"
 
 namespace tarfa {
 
@@ -291,23 +292,36 @@ TARFA_DEVI float key32_value(uint32_t key) {
   return Elem<T>::bits_to_f((uint16_t)u);
 }
 
+// Logit spread (max - min) up to which every probability of the token is a
+// normal fp32 number, so equal and distinct logits give equal and distinct
+// probabilities in the same order.
+constexpr float kTieNarrowSpread = 80.f;
+
 // One warp: softmax + top-k over E <= 32 * NPL logits of one token (values in
 // the model dtype, held as fp32).  Selection is a warp max-reduction
 // (redux.sync) of 32-bit keys per step; only the lane that owned the winner
-// rescans its NPL keys.  idx_smem (optional) receives the ids as well.
+// rescans its NPL keys (for the largest one below the winner: every larger key
+// was taken before).  When two of the top K + 1 values are equal, the ids and
+// their order are those of the reference's torch.topk (topk_ties.cuh); tie
+// (tie_scratch_ints(E) shared ints of this warp) is its working space.
+// idx_smem (optional) receives the ids as well.
 template <typename T, int NPL>
 TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float* topw,
-                            int64_t* idx_out, float* w_out, int32_t* idx_smem) {
+                            int64_t* idx_out, float* w_out, int32_t* idx_smem, uint32_t* tie) {
   const int lane = threadIdx.x & 31;
   uint32_t key[NPL];
-  uint32_t best = 0;
+  uint32_t best = 0, low = 0xffffffffu;
 #pragma unroll
   for (int j = 0; j < NPL; ++j) {
     const int e = j * 32 + lane;
     key[j] = e < E ? topk_key32<T>(__ldcg(lg + e), e) : 0u;
     best = max(best, key[j]);
+    if (e < E) low = min(low, key[j]);
   }
   const float m = key32_value<T>(__reduce_max_sync(0xffffffffu, best));
+  // Probabilities below ~2^-115 may round to equal (or zero) values for
+  // different logits: then only the fp32 probabilities give the reference's ties.
+  const bool wide = m - key32_value<T>(__reduce_min_sync(0xffffffffu, low)) > kTieNarrowSpread;
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < NPL; ++j)
@@ -316,18 +330,36 @@ TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float
   for (int d = 16; d; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
   int my_e = 0;
   float my_v = 0.f;
-  for (int k = 0; k < K; ++k) {
+  uint32_t prev = 0;
+  bool tied = false;
+  const int rounds = K < E ? K + 1 : K;    // one more to see a tie at the boundary
+  for (int k = 0; k < rounds; ++k) {
     const uint32_t kk = __reduce_max_sync(0xffffffffu, best);
+    if (k > 0) tied |= (kk >> 16) == (prev >> 16);
+    prev = kk;
+    if (k == K) break;
     const int e = (int)(0xFFFFu - (kk & 0xFFFFu));
     if (lane == k) { my_e = e; my_v = key32_value<T>(kk); }
     if ((e & 31) == lane) {
       best = 0;
 #pragma unroll
-      for (int j = 0; j < NPL; ++j) {
-        if (j == (e >> 5)) key[j] = 0u;
-        best = max(best, key[j]);
-      }
+      for (int j = 0; j < NPL; ++j)
+        if (key[j] < kk) best = max(best, key[j]);
     }
+  }
+  if (tied || wide) {
+    // the values in sorted order are the same; which ids carry them is not
+    TieElem* row = tie_row(tie);
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const int e = j * 32 + lane;
+      if (e < E)
+        row[e] = tie_elem(wide ? __float_as_uint(__fdiv_rn(expf(key32_value<T>(key[j]) - m), s))
+                               : key[j] >> 16, e);
+    }
+    __syncwarp();
+    const int id = tie_order_ids(tie, E, K);
+    if (lane < K) my_e = id;
   }
   // softmax probabilities of the selected (fp32), renormalised over the k
   // (modeling_qwen3_5_moe.py:766-768); K <= 32
@@ -349,15 +381,16 @@ TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float
 template <typename T>
 __device__ __noinline__ void warp_topk_wide(const float* lg, int E, int K, int32_t* idx32,
                                             float* topw, int64_t* idx_out, float* w_out,
-                                            int32_t* idx_smem) {
-  warp_topk_n<T, 32>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
+                                            int32_t* idx_smem, uint32_t* tie) {
+  warp_topk_n<T, 32>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie);
 }
 
+// tie: this warp's tie_scratch_ints(E) shared ints.
 template <typename T>
 TARFA_DEVI void warp_topk(const float* lg, int E, int K, int32_t* idx32, float* topw,
-                          int64_t* idx_out, float* w_out, int32_t* idx_smem = nullptr) {
-  if (E <= 256) warp_topk_n<T, 8>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
-  else warp_topk_wide<T>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem);
+                          int64_t* idx_out, float* w_out, int32_t* idx_smem, uint32_t* tie) {
+  if (E <= 256) warp_topk_n<T, 8>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie);
+  else warp_topk_wide<T>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie);
 }
 
 // Permute for one token whose K routes name K distinct experts (the router's
@@ -387,115 +420,6 @@ TARFA_DEVI void warp_permute_one_token(const int32_t* idx, int K, int E, bool ad
       o.perm_tok[K] = 0;
     }
   }
-}
-
-// ---------------------------------------------------------------------------
-// in-kernel routing for decode batches
-// ---------------------------------------------------------------------------
-// The decode GEMV computes top-k and permute itself, in every CTA, from the
-// logits the router kernel wrote: no serial tail in the router, and the
-// routing of a few tokens costs one L2 read and ~1 us of warp work per CTA.
-// CTA 0 also writes the global copies the later kernels read.
-//
-// The router's own top-k names K distinct valid experts per token, so the
-// routed rows are exactly T*K and the shared-expert unit is fixed before the
-// routing is known: rows [T*K, T*K + T), token t at row T*K + t.
-struct DecodeRoute {
-  const float* logits;   // [T, E] correctly rounded logits (+ bias) from the router kernel
-  int T, K;
-  int add_shared;
-  int32_t* g_units;      // global copies for the kernels that follow (written by CTA 0)
-  int32_t* g_perm_tok;
-  int32_t* g_perm_slot;
-  int32_t* g_route_row;
-  int32_t* g_idx32;
-  float* g_topw;
-  int64_t* idx_out;      // optional user outputs
-  float* w_out;
-};
-
-// Shared-memory ints cta_route needs (a multiple of 4, so what follows stays 16-byte aligned).
-__host__ __device__ inline int route_smem_ints(int T, int K, int E, int nwarps) {
-  const int R = T * K, Umax = (R < E ? R : E);
-  const int n = 2 * R + (4 + 4 * (Umax + 1)) + (R + T) + 2 * R +
-                (T > 1 ? (int)permute_smem_ints(nwarps, E) : 0);
-  return (n + 3) & ~3;
-}
-
-struct RouteSmem {
-  int32_t* idx;
-  float* topw;
-  int32_t* units;
-  int32_t* perm_tok;
-  int32_t* perm_slot;
-  int32_t* route_row;
-  int* scratch;
-};
-
-TARFA_DEVI RouteSmem route_smem_carve(int* smem, int T, int K, int E) {
-  const int R = T * K, Umax = (R < E ? R : E);
-  RouteSmem m;
-  m.idx = smem;
-  m.topw = reinterpret_cast<float*>(smem + R);
-  m.units = smem + 2 * R;
-  m.perm_tok = m.units + 4 + 4 * (Umax + 1);
-  m.perm_slot = m.perm_tok + R + T;
-  m.route_row = m.perm_slot + R;
-  m.scratch = m.route_row + R;
-  return m;
-}
-
-// Top-k of every token and permute into shared memory (all threads of the CTA).
-template <typename T>
-TARFA_DEVI void cta_route_body(const DecodeRoute& r, int E, const RouteSmem& m, unsigned* status) {
-  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const bool pub = blockIdx.x == 0;
-  for (int t = warp; t < r.T; t += nw)
-    warp_topk<T>(r.logits + (int64_t)t * E, E, r.K, m.idx + t * r.K, m.topw + t * r.K,
-                 pub && r.idx_out ? r.idx_out + (int64_t)t * r.K : nullptr,
-                 pub && r.w_out ? r.w_out + (int64_t)t * r.K : nullptr, nullptr);
-  __syncthreads();
-  const PermuteOut o{nullptr, m.perm_tok, m.perm_slot, m.route_row, m.units, nullptr};
-  if (r.T == 1) {
-    if (warp == 0) warp_permute_one_token(m.idx, r.K, E, r.add_shared != 0, o);
-  } else {
-    block_permute<int32_t>(m.idx, r.T, r.K, E, r.add_shared != 0, o, m.scratch, status);
-  }
-  __syncthreads();
-}
-
-template <typename T>
-__device__ __noinline__ void cta_route_call(const DecodeRoute& r, int E, const RouteSmem& m,
-                                            unsigned* status) {
-  cta_route_body<T>(r, E, m, status);
-}
-
-// CTA-wide: wait for the router kernel, top-k every token, permute into shared
-// memory; CTA 0 publishes the global copies.  All threads must call it.
-// CALL: run the routing as a separate (not inlined) function.  The GEMV's hot
-// loop is sensitive to the code around it: measured on the config-1 layer,
-// inlining is faster for the one-token-block kernels (T <= 8: 53 vs 57 us at
-// T = 1) and a call faster for the two-block kernels (T = 16: 375 vs 420 us).
-template <typename T, bool CALL>
-TARFA_DEVI RouteSmem cta_route(const DecodeRoute& r, int E, int* smem, unsigned* status) {
-  const RouteSmem m = route_smem_carve(smem, r.T, r.K, E);
-  grid_dep_wait();
-  if (CALL) cta_route_call<T>(r, E, m, status);
-  else cta_route_body<T>(r, E, m, status);
-  if (blockIdx.x == 0) {
-    const int R = r.T * r.K;
-    const int nunits = m.units[0] + (m.units[2] ? 1 : 0);
-    for (int i = threadIdx.x; i < 4 + 4 * nunits; i += blockDim.x) r.g_units[i] = m.units[i];
-    for (int i = threadIdx.x; i < R + (r.add_shared ? r.T : 0); i += blockDim.x)
-      r.g_perm_tok[i] = m.perm_tok[i];
-    for (int i = threadIdx.x; i < R; i += blockDim.x) {
-      r.g_perm_slot[i] = m.perm_slot[i];
-      r.g_route_row[i] = m.route_row[i];
-      r.g_idx32[i] = m.idx[i];
-      r.g_topw[i] = m.topw[i];
-    }
-  }
-  return m;
 }
 
 }  // namespace tarfa

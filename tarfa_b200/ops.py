@@ -141,7 +141,8 @@ def router_topk(h: torch.Tensor, w_r: torch.Tensor, top_k: int, bias: torch.Tens
     """``Qwen3_5MoeTopKRouter.forward`` on the device: ``(top_k_index int64, top_k_weights fp32)``.
 
     Logits are correctly rounded model-dtype values of ``h @ w_r.T`` (+ ``bias``);
-    ties broken by ascending expert id.
+    equal values are ordered as the reference's ``torch.topk`` orders them on
+    the CPU.
     """
     _need_cuda(h, w_r, bias)
     T, H = h.shape
@@ -381,15 +382,10 @@ def set_gemm_min_tokens(tokens: int) -> None:
     api.check(api.lib().tarfa_b200_set_gemm_min_tokens(int(tokens)))
 
 
-def set_fused_decode_max_tokens(tokens: int) -> None:
-    """``moe_layer`` runs batches of 1..``tokens`` (<= 16) as one persistent
-    kernel; 0 selects the multi-kernel sequence (process-wide, default 0)."""
-    api.check(api.lib().tarfa_b200_set_fused_decode_max_tokens(int(tokens)))
-
-
 def set_decode_routing_max_tokens(tokens: int) -> None:
-    """``moe_layer`` routes batches of 1..``tokens`` (<= 16) inside the expert
-    GEMV; 0 uses the router kernel's own top-k (process-wide, default 16)."""
+    """``moe_layer`` runs batches of 1..``tokens`` (<= 16) as one chain of
+    programmatic dependent launches; 0 launches the kernels one after the
+    other (process-wide, default 16)."""
     api.check(api.lib().tarfa_b200_set_decode_routing_max_tokens(int(tokens)))
 
 
