@@ -138,7 +138,7 @@ int noalloc_scratch(void** out) {
 // ---------------------------------------------------------------------------
 struct Ws {
   size_t counter, logits, gate_logit, idx32, topw, units, perm_tok, perm_slot, route_row, act, y,
-      xperm, bar, hb_cnt, wnorm, lgpart, phist, fxlist, fxcnt;
+      xperm, bar, hb_cnt, wnorm, lgpart, phist, fxlist, fxcnt, pend;
   size_t total;
 };
 
@@ -185,6 +185,7 @@ Ws layout(const tarfa_moe_shape& s, int op) {
   if (op == TARFA_OP_MOE_LAYER || op == TARFA_OP_ROUTER) {
     w.logits = take(T * E * 4);
     w.gate_logit = take(T * 4);
+    w.pend = take(T * 4);
     w.wnorm = take(E * 4);
     // fp32 partial logits of the tensor-core router (large batches only)
     if (T >= kRouterGemmMinTokens) {
@@ -519,16 +520,26 @@ CombineArgs make_combine_args(const tarfa_moe_shape& s, const Ws& L, void* ws, c
 }
 
 template <typename T>
+// pend / idx_out (decode chain): tokens whose tie order the router left open get
+// it here (combine_token_kernel), and their ids are rewritten in idx_out.
 int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* top_w, bool int4,
-                bool with_shared, bool gemm_y, void* out, cudaStream_t st, bool pdl = false) {
+                bool with_shared, bool gemm_y, void* out, cudaStream_t st, bool pdl = false,
+                bool pend = false, int64_t* idx_out = nullptr) {
   const int T_ = (int)s.tokens, H = (int)s.hidden;
-  const CombineArgs c = make_combine_args(s, L, ws, top_w, int4, with_shared, out);
+  CombineArgs c = make_combine_args(s, L, ws, top_w, int4, with_shared, out);
+  size_t smem = 0;
+  if (pend) {
+    c.pend = at<int32_t>(ws, L.pend);
+    c.logits = at<float>(ws, L.logits);
+    c.idx_out = idx_out;
+    smem = (size_t)tie_scratch_ints(c.E) * sizeof(int);
+  }
   // large batches: one block per token; decode: one-warp blocks, so that the
   // few tokens' columns spread over many SMs (the loads are latency-bound)
   const int threads = T_ > 64 ? kCombineTokenThreads : 32;
   const dim3 grid(T_ > 64 ? 1 : (H / 8 + threads - 1) / threads, T_);
-  if (gemm_y) TARFA_CUDA(launch_k(combine_token_kernel<T, T>, grid, dim3(threads), 0, st, pdl, c));
-  else TARFA_CUDA(launch_k(combine_token_kernel<T, float>, grid, dim3(threads), 0, st, pdl, c));
+  if (gemm_y) TARFA_CUDA(launch_k(combine_token_kernel<T, T>, grid, dim3(threads), smem, st, pdl, c));
+  else TARFA_CUDA(launch_k(combine_token_kernel<T, float>, grid, dim3(threads), smem, st, pdl, c));
   TARFA_CUDA(cudaGetLastError());
   stage_mark(4, st);
   return TARFA_OK;
@@ -675,9 +686,9 @@ bool use_decode_routing(const tarfa_moe_shape& s, const tarfa_moe_weights& w) {
          !use_gemm(s, w, s.shared_inter);
 }
 
-template <typename T>
 // route: the last CTA also runs top-k and permute into the workspace (decode
 // chain); idx_out / w_out receive the routing then.
+template <typename T>
 int launch_router_logits(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
                          const void* bias, const void* w_sg, const Ws& L, void* ws, int sms,
                          cudaStream_t st, bool route = false, int64_t* idx_out = nullptr,
@@ -695,6 +706,7 @@ int launch_router_logits(const tarfa_moe_shape& s, const void* hidden, const voi
     a.perm = PermuteOut{nullptr, at<int32_t>(ws, L.perm_tok), at<int32_t>(ws, L.perm_slot),
                         at<int32_t>(ws, L.route_row), at<int32_t>(ws, L.units), nullptr};
     a.status = status;
+    a.pend = at<int32_t>(ws, L.pend);   // interior ties: order settled by the combine
   }
   a.h = hidden;
   a.w_r = w_r;
@@ -745,7 +757,7 @@ int run_decode_layer(const tarfa_moe_shape& s, const void* hidden, const void* w
   stage_mark(1, st);
   if (int rc = run_experts<T>(s, hidden, w, sh, L, ws, out, status, sms, st, true)) return rc;
   return run_combine<T>(s, L, ws, at<float>(ws, L.topw), w.kind == TARFA_W_INT4, sh != nullptr,
-                        false, out, st, true);
+                        false, out, st, true, true, idx_out);
 }
 
 // ===========================================================================

@@ -16,6 +16,9 @@ struct CombineArgs {
   const float* gate_logit; // [T] or null: add the gated shared expert
   const int32_t* units;    // unit table: units[3] = first shared-expert row
   void* out;               // [T, H] model dtype
+  const int32_t* pend;     // [T] or null: tokens whose tie order the router left open
+  const float* logits;     // [T, E] router logits (with pend)
+  int64_t* idx_out;        // optional [T, K]: rewritten in the reference's order (with pend)
 };
 
 }  // namespace tarfa

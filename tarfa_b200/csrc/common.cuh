@@ -8,6 +8,11 @@
 
 #define TARFA_DEVI __device__ __forceinline__
 
+// Phase marks for timing probes built outside the library (no-ops here).
+#ifndef TARFA_PHASE
+#define TARFA_PHASE(i)
+#endif
+
 namespace tarfa {
 
 // ---------------------------------------------------------------------------

@@ -212,6 +212,59 @@ TARFA_DEVI float gate_up_act(float g, float u) {
   return rnd<T>(silu_f(gr)) * ur;
 }
 
+// A resolved tile: the unit, its 16 weight rows for fragment rows g and g + 8
+// (byte pointers) and the int4 scale rows.
+struct GemvTile {
+  bool shared_unit;
+  int tt, K;
+  UnitDesc d;
+  const char* rowA;
+  const char* rowB;
+  const void* scA;
+  const void* scB;
+};
+
+template <typename T, int MODE, int PHASE>
+TARFA_DEVI GemvTile gemv_tile(const GemvArgs& a, int tile, int nt_s, int tiles_r,
+                              const int32_t* units, int nu, const UnitDesc& fixed_sh, int g) {
+  constexpr bool INT4 = MODE != kModeExact;
+  GemvTile r;
+  r.scA = r.scB = nullptr;
+  if (tile >= nt_s) {
+    const int u = (tile - nt_s) / tiles_r;
+    r.shared_unit = false;
+    r.tt = (tile - nt_s) % tiles_r;
+    r.d = unit_descs(units)[u];
+    const int slot = a.expert_slot ? a.expert_slot[r.d.expert] : r.d.expert;
+    r.K = a.K_r;
+    const int ra = PHASE == kGateUp ? r.tt * 8 + g : r.tt * 16 + g;
+    const int rb = PHASE == kGateUp ? a.N_r + r.tt * 8 + g : r.tt * 16 + g + 8;
+    const int64_t esz = INT4 ? 4 : (int64_t)sizeof(T);
+    const char* wb = static_cast<const char*>(a.w) + (int64_t)slot * a.w_estride * esz;
+    r.rowA = wb + (int64_t)ra * a.w_rstride * esz;
+    r.rowB = wb + (int64_t)rb * a.w_rstride * esz;
+    if (INT4) {
+      const T* sb = static_cast<const T*>(a.sc) + (int64_t)slot * a.s_estride;
+      r.scA = sb + (int64_t)ra * a.s_rstride;
+      r.scB = sb + (int64_t)rb * a.s_rstride;
+    }
+  } else {
+    r.shared_unit = true;
+    r.tt = tile;
+    r.d = a.route_mode != 0 ? fixed_sh : unit_descs(units)[nu];
+    r.K = a.K_s;
+    const T* s0 = static_cast<const T*>(a.sw0);
+    if (PHASE == kGateUp) {
+      r.rowA = reinterpret_cast<const char*>(s0 + (int64_t)(r.tt * 8 + g) * r.K);
+      r.rowB = reinterpret_cast<const char*>(static_cast<const T*>(a.sw1) + (int64_t)(r.tt * 8 + g) * r.K);
+    } else {
+      r.rowA = reinterpret_cast<const char*>(s0 + (int64_t)(r.tt * 16 + g) * r.K);
+      r.rowB = reinterpret_cast<const char*>(s0 + (int64_t)(r.tt * 16 + g + 8) * r.K);
+    }
+  }
+  return r;
+}
+
 template <typename T, int MODE, int PHASE, int KSPLIT, int NTB>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a) {
   constexpr bool INT4 = MODE != kModeExact;
@@ -223,13 +276,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   const int grp = warp / KSPLIT, kw = warp % KSPLIT;
   const int g = lane >> 2, c = lane & 3;
 
-  grid_dep_launch_dependents();
+  // Mode 0 releases its dependents only once the kernel before it has
+  // completed: the decode chain's combine reads the router's logits before its
+  // own wait, so they must be complete when it starts.
+  if (a.route_mode != 0) grid_dep_launch_dependents();
   const int32_t* units = a.units;
   const int32_t* const perm_tok = a.perm_tok;
   int nu = -1;          // routed units; unknown until the unit table is there (mode 3)
   bool has_sh;
   if (a.route_mode == 0) {
     grid_dep_wait();
+    grid_dep_launch_dependents();
     nu = units[0];
     has_sh = units[2] != 0;
   } else {
@@ -253,45 +310,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
     if (base >= ntiles) break;
     const int tile = base + grp;
     if (tile >= ntiles) continue;   // uniform within a warp group; groups sync separately
-    // -------- resolve the tile ------------------------------------------------
-    bool shared_unit = false;
-    int tt = 0, K = 0;
-    UnitDesc d;
-    const char* rowA = nullptr;   // weight row for fragment rows g   (bytes)
-    const char* rowB = nullptr;   // weight row for fragment rows g+8
-    const T* scA = nullptr;       // int4 scale rows
-    const T* scB = nullptr;
-    if (tile >= nt_s) {
-      const int u = (tile - nt_s) / tiles_r;
-      tt = (tile - nt_s) % tiles_r;
-      d = unit_descs(units)[u];
-      const int slot = a.expert_slot ? a.expert_slot[d.expert] : d.expert;
-      K = a.K_r;
-      const int ra = PHASE == kGateUp ? tt * 8 + g : tt * 16 + g;
-      const int rb = PHASE == kGateUp ? a.N_r + tt * 8 + g : tt * 16 + g + 8;
-      const int64_t esz = INT4 ? 4 : (int64_t)sizeof(T);
-      const char* wb = static_cast<const char*>(a.w) + (int64_t)slot * a.w_estride * esz;
-      rowA = wb + (int64_t)ra * a.w_rstride * esz;
-      rowB = wb + (int64_t)rb * a.w_rstride * esz;
-      if (INT4) {
-        const T* sb = static_cast<const T*>(a.sc) + (int64_t)slot * a.s_estride;
-        scA = sb + (int64_t)ra * a.s_rstride;
-        scB = sb + (int64_t)rb * a.s_rstride;
-      }
-    } else {
-      shared_unit = true;
-      tt = tile;
-      d = a.route_mode != 0 ? fixed_sh : unit_descs(units)[nu];
-      K = a.K_s;
-      const T* s0 = static_cast<const T*>(a.sw0);
-      if (PHASE == kGateUp) {
-        rowA = reinterpret_cast<const char*>(s0 + (int64_t)(tt * 8 + g) * K);
-        rowB = reinterpret_cast<const char*>(static_cast<const T*>(a.sw1) + (int64_t)(tt * 8 + g) * K);
-      } else {
-        rowA = reinterpret_cast<const char*>(s0 + (int64_t)(tt * 16 + g) * K);
-        rowB = reinterpret_cast<const char*>(s0 + (int64_t)(tt * 16 + g + 8) * K);
-      }
-    }
+    const GemvTile tl = gemv_tile<T, MODE, PHASE>(a, tile, nt_s, tiles_r, units, nu, fixed_sh, g);
+    const bool shared_unit = tl.shared_unit;
+    const int tt = tl.tt, K = tl.K;
+    const UnitDesc d = tl.d;
+    const char* rowA = tl.rowA;
+    const char* rowB = tl.rowB;
+    const T* scA = static_cast<const T*>(tl.scA);
+    const T* scB = static_cast<const T*>(tl.scB);
     const int ntok = d.nrows;
     const int ntb_groups = (ntok + 8 * NTB - 1) / (8 * NTB);
 

@@ -304,17 +304,23 @@ constexpr float kTieNarrowSpread = 80.f;
 // was taken before).  When two of the top K + 1 values are equal, the ids and
 // their order are those of the reference's torch.topk (topk_ties.cuh); tie
 // (tie_scratch_ints(E) shared ints of this warp) is its working space.
-// idx_smem (optional) receives the ids as well.
-template <typename T, int NPL>
+// pend (optional): a tie strictly inside the top K leaves the set of experts
+// as it is, so the reference's order is then left to a later kernel
+// (warp_tie_order): the ids come out by (value, id) and *pend is set to 1
+// (else 0).  idx_smem (optional) receives the ids as well.
+// SMEM_LG: lg is in this CTA's shared memory (else global, read through L2:
+// other CTAs of the kernel wrote it).
+template <typename T, int NPL, bool SMEM_LG = false>
 TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float* topw,
-                            int64_t* idx_out, float* w_out, int32_t* idx_smem, uint32_t* tie) {
+                            int64_t* idx_out, float* w_out, int32_t* idx_smem, uint32_t* tie,
+                            int32_t* pend = nullptr) {
   const int lane = threadIdx.x & 31;
   uint32_t key[NPL];
   uint32_t best = 0, low = 0xffffffffu;
 #pragma unroll
   for (int j = 0; j < NPL; ++j) {
     const int e = j * 32 + lane;
-    key[j] = e < E ? topk_key32<T>(__ldcg(lg + e), e) : 0u;
+    key[j] = e < E ? topk_key32<T>(SMEM_LG ? lg[e] : __ldcg(lg + e), e) : 0u;
     best = max(best, key[j]);
     if (e < E) low = min(low, key[j]);
   }
@@ -328,14 +334,16 @@ TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float
     if (j * 32 + lane < E) s += expf(key32_value<T>(key[j]) - m);
 #pragma unroll
   for (int d = 16; d; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+  TARFA_PHASE(5);
   int my_e = 0;
   float my_v = 0.f;
   uint32_t prev = 0;
-  bool tied = false;
+  bool tied = false, boundary = false;
   const int rounds = K < E ? K + 1 : K;    // one more to see a tie at the boundary
   for (int k = 0; k < rounds; ++k) {
     const uint32_t kk = __reduce_max_sync(0xffffffffu, best);
     if (k > 0) tied |= (kk >> 16) == (prev >> 16);
+    if (k == K) boundary = (kk >> 16) == (prev >> 16);
     prev = kk;
     if (k == K) break;
     const int e = (int)(0xFFFFu - (kk & 0xFFFFu));
@@ -347,7 +355,10 @@ TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float
         if (key[j] < kk) best = max(best, key[j]);
     }
   }
-  if (tied || wide) {
+  TARFA_PHASE(6);
+  const bool defer = pend && tied && !boundary && !wide;
+  if (pend && lane == 0) *pend = defer ? 1 : 0;
+  if ((tied || wide) && !defer) {
     // the values in sorted order are the same; which ids carry them is not
     TieElem* row = tie_row(tie);
 #pragma unroll
@@ -361,6 +372,7 @@ TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float
     const int id = tie_order_ids(tie, E, K);
     if (lane < K) my_e = id;
   }
+  TARFA_PHASE(7);
   // softmax probabilities of the selected (fp32), renormalised over the k
   // (modeling_qwen3_5_moe.py:766-768); K <= 32
   const float p = lane < K ? __fdiv_rn(expf(my_v - m), s) : 0.f;
@@ -381,16 +393,37 @@ TARFA_DEVI void warp_topk_n(const float* lg, int E, int K, int32_t* idx32, float
 template <typename T>
 __device__ __noinline__ void warp_topk_wide(const float* lg, int E, int K, int32_t* idx32,
                                             float* topw, int64_t* idx_out, float* w_out,
-                                            int32_t* idx_smem, uint32_t* tie) {
-  warp_topk_n<T, 32>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie);
+                                            int32_t* idx_smem, uint32_t* tie, int32_t* pend) {
+  warp_topk_n<T, 32>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie, pend);
 }
 
-// tie: this warp's tie_scratch_ints(E) shared ints.
+// tie: this warp's tie_scratch_ints(E) shared ints; pend: see warp_topk_n.
 template <typename T>
 TARFA_DEVI void warp_topk(const float* lg, int E, int K, int32_t* idx32, float* topw,
-                          int64_t* idx_out, float* w_out, int32_t* idx_smem, uint32_t* tie) {
-  if (E <= 256) warp_topk_n<T, 8>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie);
-  else warp_topk_wide<T>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie);
+                          int64_t* idx_out, float* w_out, int32_t* idx_smem, uint32_t* tie,
+                          int32_t* pend = nullptr) {
+  if (E <= 256) warp_topk_n<T, 8>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie, pend);
+  else warp_topk_wide<T>(lg, E, K, idx32, topw, idx_out, w_out, idx_smem, tie, pend);
+}
+
+// The reference's order of a token whose top K has a tie inside it (warp_topk_n
+// deferred it): lane j < K returns the id at place j.  Same logits, same set.
+template <typename T, int NPL>
+TARFA_DEVI int warp_tie_order_n(const float* lg, int E, int K, uint32_t* tie) {
+  const int lane = threadIdx.x & 31;
+  TieElem* row = tie_row(tie);
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    const int e = j * 32 + lane;
+    if (e < E) row[e] = tie_elem(topk_key32<T>(__ldcg(lg + e), e) >> 16, e);
+  }
+  __syncwarp();
+  return tie_order_ids(tie, E, K);
+}
+
+template <typename T>
+TARFA_DEVI int warp_tie_order(const float* lg, int E, int K, uint32_t* tie) {
+  return E <= 256 ? warp_tie_order_n<T, 8>(lg, E, K, tie) : warp_tie_order_n<T, 32>(lg, E, K, tie);
 }
 
 // Permute for one token whose K routes name K distinct experts (the router's
