@@ -12,7 +12,7 @@ import threading
 
 from . import build as _build
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 TARFA_OK, TARFA_ERR_INVALID, TARFA_ERR_UNSUPPORTED, TARFA_ERR_WORKSPACE, TARFA_ERR_CUDA = range(5)
 TARFA_BF16, TARFA_F16 = 0, 1
@@ -30,7 +30,7 @@ class MoeShape(C.Structure):
 class MoeWeights(C.Structure):
     _fields_ = [("kind", C.c_int32), ("group", C.c_int32), ("gate_up", C.c_void_p),
                 ("gate_up_scale", C.c_void_p), ("down", C.c_void_p),
-                ("down_scale", C.c_void_p), ("expert_slot", C.c_void_p)]
+                ("down_scale", C.c_void_p), ("expert_slot", C.c_void_p), ("slots", C.c_int64)]
 
 
 class SharedExpert(C.Structure):

@@ -232,6 +232,7 @@ int check_weights(const tarfa_moe_shape* s, const tarfa_moe_weights* w) {
   TARFA_CHECK(w, "null weights");
   TARFA_CHECK(w->gate_up && w->down, "null expert weights");
   TARFA_CHECK(aligned16(w->gate_up) && aligned16(w->down), "expert weights not 16-byte aligned");
+  TARFA_CHECK(!w->expert_slot || w->slots >= 1, "expert_slot needs slots (the weight stacks' depth)");
   if (w->kind == TARFA_W_INT4) {
     TARFA_CHECK(w->gate_up_scale && w->down_scale, "int4 weights need scales");
     TARFA_CHECK(s->hidden % 128 == 0 && s->inter % 128 == 0,
@@ -369,7 +370,7 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
     p.T = T_;
     p.H = H;
     p.E = E;
-    p.E_store = E;
+    p.E_store = w.expert_slot ? w.slots : E;   // the TMA maps cover every slot
     p.I = I;
     p.Is = Is;
     p.rows_total = R + (Is ? T_ : 0);

@@ -88,13 +88,19 @@ class ExpertWeights:
         if self.expert_slot is not None and self.expert_slot.dtype != torch.int32:
             raise RuntimeError("expert_slot must be int32")
         return api.MoeWeights(kind, int(self.group), _ptr(self.gate_up), _ptr(self.gate_up_scale),
-                              _ptr(self.down), _ptr(self.down_scale), _ptr(self.expert_slot))
+                              _ptr(self.down), _ptr(self.down_scale), _ptr(self.expert_slot),
+                              self.slots() if self.expert_slot is not None else 0)
 
     def dims(self, H: int):
-        """(E, I) inferred from the stacks."""
-        E = self.gate_up.shape[0]
+        """(E, I): with an ``expert_slot`` table, E is its length (the layer's
+        experts; the stacks hold any number of slots), else the stacks' depth."""
+        E = self.expert_slot.numel() if self.expert_slot is not None else self.gate_up.shape[0]
         I = self.gate_up.shape[1] // 2
         return E, I
+
+    def slots(self) -> int:
+        """Depth of the weight stacks (slots the kernels may read)."""
+        return self.gate_up.shape[0]
 
 
 @dataclasses.dataclass
@@ -113,22 +119,26 @@ class SharedWeights:
 
 def _check_weights(w: ExpertWeights, H: int, dtype):
     E, I = w.dims(H)
+    S = w.slots()
+    if w.expert_slot is not None and (w.expert_slot.dtype != torch.int32 or
+                                      w.expert_slot.device != w.gate_up.device):
+        raise RuntimeError("expert_slot must be an int32 tensor on the weights' device")
     if w.kind == "dense":
         if w.gate_up.dtype != dtype or w.down.dtype != dtype:
             raise RuntimeError("dense expert weights must be in the activation dtype")
-        if tuple(w.gate_up.shape) != (E, 2 * I, H) or tuple(w.down.shape) != (E, H, I):
+        if tuple(w.gate_up.shape) != (S, 2 * I, H) or tuple(w.down.shape) != (S, H, I):
             raise RuntimeError(f"expert weight shapes {tuple(w.gate_up.shape)} / "
                                f"{tuple(w.down.shape)} do not match H={H}")
     elif w.kind == "int4":
         for t, (n, k) in ((w.gate_up, (2 * I, H)), (w.down, (H, I))):
             if t.dtype not in (torch.int32, torch.uint8):
                 raise RuntimeError("int4 weights must be int32 or uint8 packed")
-            if t.shape[0] != E or t.shape[1] != n or t.numel() * t.element_size() != E * n * k // 2:
+            if t.shape[0] != S or t.shape[1] != n or t.numel() * t.element_size() != S * n * k // 2:
                 raise RuntimeError("int4 weight shape mismatch")
         for s, n, k in ((w.gate_up_scale, 2 * I, H), (w.down_scale, H, I)):
             if s is None or s.dtype != dtype:
                 raise RuntimeError("int4 scales must be given in the activation dtype")
-            want = E * n * (k // w.group if w.group else 1)
+            want = S * n * (k // w.group if w.group else 1)
             if s.numel() != want:
                 raise RuntimeError(f"int4 scale has {s.numel()} elements, expected {want}")
     else:

@@ -1,15 +1,21 @@
 """Synthetic MoE-only decoder stack for whole-model measurements.
 
-``n_layers`` x (``h = h + MoE(RMSNorm(h))``) between an embedding and an fp32
-LM head with greedy argmax: the MoE path of the reference's decoder layer
+``n_layers`` x (``h = h + MoE(RMSNorm(h))``) between an embedding and an LM
+head with greedy argmax: the MoE path of the reference's decoder layer
 (``modeling_qwen3_5_moe.py:828-870``: post-attention RMSNorm, sparse MoE block,
-residual) with attention left out, and the reference's fp32 final logits
-(``serve.py:128-132``).  Weights are synthetic, regenerable per (layer, expert)
+residual) with attention left out; the reference takes its final logits in fp32
+(``serve.py:128-132``), this stack in fp64 (below).  Weights are synthetic, regenerable per (layer, expert)
 (``tarfa_b200.synthetic``); the routed experts come from a
 ``StreamingExpertTier`` (resident + pinned-host streaming) or are all resident.
 
-RMSNorm follows ``Qwen3_5MoeRMSNorm`` (modeling_qwen3_5_moe.py:795-808):
-``(x.float() * rsqrt(mean(x^2) + eps) * (1 + w)).to(x.dtype)``.
+RMSNorm follows ``Qwen3_5MoeRMSNorm`` (modeling_qwen3_5_moe.py:795-808),
+``x * rsqrt(mean(x^2) + eps) * (1 + w)`` rounded to the model dtype, but in
+fp64 with the squares summed by a fixed pairwise tree of elementwise adds:
+IEEE additions, division and square root in a fixed order give the CUDA stack
+and the CPU oracle stack the same bits (a library reduction would depend on its
+order and on the device's rsqrt).  The LM head is fp64 (its argmax is the
+greedy token; summation order moves its logits by ~1e-16 relative).  These two are the synthetic skeleton around
+the MoE blocks, not part of the path under test.
 """
 from __future__ import annotations
 
@@ -20,9 +26,28 @@ from . import synthetic as syn
 from .streaming import StreamingExpertTier
 
 
+def _tree_sum(v: torch.Tensor) -> torch.Tensor:
+    """Sum over the last dimension by a fixed pairwise tree of elementwise adds
+    (halves while even, then left to right): the same additions in the same
+    order on every device."""
+    while v.shape[-1] > 1 and v.shape[-1] % 2 == 0:
+        n = v.shape[-1] // 2
+        v = v[..., :n] + v[..., n:]
+    acc = v[..., :1]
+    for j in range(1, v.shape[-1]):
+        acc = acc + v[..., j:j + 1]
+    return acc
+
+
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + w.float())).to(x.dtype)
+    xd = x.double()
+    r = 1.0 / torch.sqrt(_tree_sum(xd * xd) / x.shape[-1] + eps)
+    return (xd * r * (1.0 + w.double())).to(torch.float32).to(x.dtype)
+
+
+def lm_head_argmax(h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Greedy token: argmax of the fp64 logits h @ w.T."""
+    return (h.double() @ w.double().t()).argmax(-1)
 
 
 class SyntheticStack:
@@ -55,6 +80,10 @@ class SyntheticStack:
             del L
         self._prev = [None] * n_layers
 
+    def expert_cpu(self, l: int, e: int):
+        """(gate_up, down) of expert ``e`` of layer ``l`` on the CPU (for the oracle)."""
+        return self.tier.expert_cpu(l, e)
+
     def layer_weights_cpu(self, l: int):
         """(gate_up, down) of all experts of layer l, on the CPU (for the oracle)."""
         R = self.tier.R
@@ -82,6 +111,4 @@ class SyntheticStack:
             self._prev[l] = ids
             routed = ops.experts_forward(x, idx, w, weights)
             h = h + (routed + ops.shared_expert(x, layer["shared"]))
-        hf = rms_norm(h, self.final_norm)
-        logits = hf.float() @ self.lm_head.float().t()          # fp32 logits
-        return logits.argmax(-1)
+        return lm_head_argmax(rms_norm(h, self.final_norm), self.lm_head)
