@@ -303,7 +303,7 @@ template <typename T, int MODE, int PHASE, int KSPLIT, int NTB>
 int launch_gemv(const GemvArgs& a, int max_tiles, int sms, cudaStream_t st, bool pdl, int smem) {
   constexpr int groups = kGemvWarps / KSPLIT;
   int grid = (max_tiles + groups - 1) / groups;
-  const int cap = 2 * sms;
+  const int cap = gemv_ctas_per_sm(MODE, PHASE, NTB) * sms;
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
   TARFA_CUDA(launch_k(gemv_kernel<T, MODE, PHASE, KSPLIT, NTB>, dim3(grid), dim3(kGemvThreads),
@@ -326,16 +326,18 @@ constexpr int kKsplitDown = 2;
 // int4 tiles hold a quarter of the bytes of dense ones, so fewer warps share a
 // tile's K (the per-tile reduction and epilogue amortise over more data).
 // Measured on the config-1 layer (group 128): gate_up split 4 at 1-2 tokens
-// (51 vs 59 us per layer at T = 1), 2 from 4 tokens (313 vs 363 us at T = 16);
+// (45.8 vs 48.8 us per layer at T = 1 against split 2), 2 from 4 tokens;
 // down split 2.
 
 // T_: tokens of the batch (picks the K split, which fixes the fp32 summation
 // order); rows: most rows of one unit (picks the token blocks; -1: T_).
+constexpr int q4_ksplit(int phase, int T_) { return phase == kGateUp && T_ <= 2 ? 4 : 2; }
+
 template <typename T, int MODE, int PHASE>
 int launch_gemv_q4(const GemvArgs& a, int max_tiles, int T_, int sms, cudaStream_t st, bool pdl,
                    int smem, int rows = -1) {
   if (rows < 0) rows = T_;
-  if (PHASE == kGateUp && T_ <= 2)
+  if (q4_ksplit(PHASE, T_) == 4)
     return launch_gemv_ntb<T, MODE, PHASE, 4>(a, max_tiles, rows, sms, st, pdl, smem);
   return launch_gemv_ntb<T, MODE, PHASE, 2>(a, max_tiles, rows, sms, st, pdl, smem);
 }
@@ -442,11 +444,15 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
     g.which = 3;
     rc = launch_gemv_ntb<T, kModeExact, kGateUp, kKsplitGateUp>(g, tiles_gu, T_, sms, st, pdl, smem);
   } else {
-    g.which = 1;
+    // The int4 kernel runs the shared expert's tiles too (first, with the exact
+    // loop) when its K split is the dense one's, so the shared expert's fp32
+    // summation order is the same as in its own launch.
+    const bool with_sh = q4_ksplit(kGateUp, T_) == kKsplitGateUp;
+    g.which = with_sh ? 3 : 1;
     rc = mode == kModeInt4Fused
              ? launch_gemv_q4<T, kModeInt4Fused, kGateUp>(g, tiles_gu, T_, sms, st, pdl, smem)
              : launch_gemv_q4<T, kModeInt4Dequant, kGateUp>(g, tiles_gu, T_, sms, st, pdl, smem);
-    if (rc == TARFA_OK && Is) {
+    if (rc == TARFA_OK && Is && !with_sh) {
       GemvArgs gs = g;
       gs.which = 2;
       if (chained) gs.route_mode = 2;   // fixed shared rows, no unit table needed
@@ -485,11 +491,12 @@ int run_experts(const tarfa_moe_shape& s, const void* hidden, const tarfa_moe_we
 
     rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(g, tiles_dn, T_, sms, st, pdl);
   } else {
-    g.which = 1;
+    const bool with_sh = q4_ksplit(kDown, T_) == kKsplitDown;
+    g.which = with_sh ? 3 : 1;
     rc = mode == kModeInt4Fused
              ? launch_gemv_q4<T, kModeInt4Fused, kDown>(g, tiles_dn, T_, sms, st, pdl, 0)
              : launch_gemv_q4<T, kModeInt4Dequant, kDown>(g, tiles_dn, T_, sms, st, pdl, 0);
-    if (rc == TARFA_OK && Is) {
+    if (rc == TARFA_OK && Is && !with_sh) {
       GemvArgs gs = g;
       gs.which = 2;
       rc = launch_gemv_ntb<T, kModeExact, kDown, kKsplitDown>(gs, H / 16, T_, sms, st, pdl);

@@ -102,10 +102,13 @@ template <> struct Mma<__nv_bfloat16> {
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
-  // (q - 8) for two packed "128 + q" halves: exact subtraction
+  // (q - 8) for two packed "128 + q" halves: (128 + q) * 1 - 136, exact.
+  // Written as a bf16x2 fused multiply-add (a native instruction since sm_80).
   TARFA_DEVI static uint32_t sub_magic(uint32_t v) {
     uint32_t r;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(Elem<__nv_bfloat16>::kMagicMinus8));
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;"
+        : "=r"(r)
+        : "r"(v), "r"(0x3F803F80u), "r"(Elem<__nv_bfloat16>::kMagicMinus8 | 0x80008000u));
     return r;
   }
   // one correctly rounded product per half

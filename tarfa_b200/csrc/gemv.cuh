@@ -39,7 +39,7 @@ struct GemvArgs {
   const void* x_sh;          // GATE_UP, or null: the shared unit's token rows (else x)
   const int32_t* perm_tok;   // GATE_UP: row -> token; DOWN: unused (row = x row)
   const int32_t* units;
-  int which;                 // bit 0: routed units, bit 1: shared unit (dense kernels only)
+  int which;                 // bit 0: routed units, bit 1: shared unit
   int E;
   const void* w;             // routed weights: GATE_UP gate_up base, DOWN down base
   int64_t w_estride;         // per expert (elements, or 32-bit words for int4)
@@ -71,14 +71,23 @@ struct GemvArgs {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
+// Resident CTAs per SM a launch is built for (registers fit it; grids are
+// capped at this many per SM).  The int4 kernels of 1-8 tokens fit three in 80
+// registers: the int4 loop is latency-bound (dequantisation between each
+// batch of loads and its MMAs), so more resident warps hide more of it
+// (config-1 layer, T = 1: 45.8 vs 47.9 us per layer).  The dense down GEMV
+// measured no better with three.
+constexpr int gemv_ctas_per_sm(int mode, int phase, int ntb) {
+  return (mode != kModeExact && ntb == 1) ? 3 : 2;
+}
 
 TARFA_DEVI void group_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // One warp's share of a 16-row tile: acc[b] += W(rows g, g+8)[k in iterations
-// [i0, i1)] . x(token block b).  An iteration is 32 k (dense) or 128 k (int4,
-// one scale group).  xrow[b] is this lane's token row (null: zero column).
+// [i0, i1)] . x(token block b).  An iteration is 32 k (dense) or 128 k (int4;
+// a scale group spans whole iterations).  xrow[b] is this lane's token row (always a valid row).
 // Dense weights are loaded 4 iterations (8 x 16 B per lane) at a time.
 template <typename T, int MODE, int NTB>
 TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, const T* scB,
@@ -101,8 +110,7 @@ TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, con
         const int64_t off = ((int64_t)(it + j) * 32 + c * 8) * (int64_t)sizeof(T);
 #pragma unroll
         for (int b = 0; b < NTB; ++b) {
-          uint4 xv = make_uint4(0, 0, 0, 0);
-          if (xrow[b]) xv = ld_cached(xrow[b] + off);
+          const uint4 xv = ld_cached(xrow[b] + off);
           Mma<T>::run(acc[b], wa[j].x, wb[j].x, wa[j].y, wb[j].y, xv.x, xv.y);
           Mma<T>::run(acc[b], wa[j].z, wb[j].z, wa[j].w, wb[j].w, xv.z, xv.w);
         }
@@ -113,8 +121,7 @@ TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, con
       const uint4 wa = ld_stream(rowA + off), wb = ld_stream(rowB + off);
 #pragma unroll
       for (int b = 0; b < NTB; ++b) {
-        uint4 xv = make_uint4(0, 0, 0, 0);
-        if (xrow[b]) xv = ld_cached(xrow[b] + off);
+        const uint4 xv = ld_cached(xrow[b] + off);
         Mma<T>::run(acc[b], wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
         Mma<T>::run(acc[b], wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
       }
@@ -122,17 +129,37 @@ TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, con
   } else {
     // lane c covers k [32c, 32c+32) of each 128-k iteration
     const bool grp_scale = group != 0;
-    constexpr int NBQ = 4;   // iterations whose weights are in flight together
+    const bool need_sc = grp_scale || MODE == kModeInt4Dequant;
+    const unsigned short* scA16 = reinterpret_cast<const unsigned short*>(scA);
+    const unsigned short* scB16 = reinterpret_cast<const unsigned short*>(scB);
+    // scale index of the next iteration: a group spans ipg iterations of 128 k
+    // (tracked by a counter; no division in the loop)
+    const int ipg = grp_scale ? group >> 7 : 0x7fffffff;
+    int g_idx = grp_scale ? i0 / ipg : 0;
+    int g_rem = grp_scale ? i0 - g_idx * ipg : 0;
+    // iterations whose weights (and scales) are in flight together (three
+    // keep the kernel in 80 registers)
+    constexpr int NBQ = 3;
     for (int ib = i0; ib < i1; ib += NBQ) {
       uint4 qa_b[NBQ], qb_b[NBQ];
+      unsigned short ua_b[NBQ], ub_b[NBQ];
 #pragma unroll
       for (int j = 0; j < NBQ; ++j) {
         qa_b[j] = make_uint4(0, 0, 0, 0);
         qb_b[j] = qa_b[j];
+        ua_b[j] = ub_b[j] = 0;
         if (ib + j < i1) {
           const int64_t woff = ((int64_t)(ib + j) * 16 + c * 4) * 4;   // bytes
           qa_b[j] = ld_stream(rowA + woff);
           qb_b[j] = ld_stream(rowB + woff);
+          if (need_sc) {
+            ua_b[j] = __ldg(scA16 + g_idx);
+            ub_b[j] = __ldg(scB16 + g_idx);
+            if (++g_rem == ipg) {
+              g_rem = 0;
+              ++g_idx;
+            }
+          }
         }
       }
 #pragma unroll
@@ -142,10 +169,9 @@ TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, con
         const uint4 qa = qa_b[j], qb = qb_b[j];
         float sa = 1.f, sb = 1.f;
         uint32_t sa2 = 0, sb2 = 0;
-        if (grp_scale || MODE == kModeInt4Dequant) {
-          const int gi = grp_scale ? (it * 128) / group : 0;
-          const uint16_t ua = reinterpret_cast<const uint16_t*>(scA)[gi];
-          const uint16_t ub = reinterpret_cast<const uint16_t*>(scB)[gi];
+        if (need_sc) {
+          const uint16_t ua = ua_b[j];
+          const uint16_t ub = ub_b[j];
           sa = Elem<T>::bits_to_f(ua);
           sb = Elem<T>::bits_to_f(ub);
           sa2 = uint32_t(ua) | (uint32_t(ua) << 16);
@@ -173,8 +199,7 @@ TARFA_DEVI void gemv_kloop(const char* rowA, const char* rowB, const T* scA, con
           const int64_t xoff = ((int64_t)it * 128 + c * 32 + m * 8) * (int64_t)sizeof(T);
 #pragma unroll
           for (int b = 0; b < NTB; ++b) {
-            uint4 xv = make_uint4(0, 0, 0, 0);
-            if (xrow[b]) xv = ld_cached(xrow[b] + xoff);
+            const uint4 xv = ld_cached(xrow[b] + xoff);
             // (x0,x4) (x1,x5) (x2,x6) (x3,x7) to match nibble pairs (s, s+4)
             const uint32_t x04 = __byte_perm(xv.x, xv.z, 0x5410);
             const uint32_t x15 = __byte_perm(xv.x, xv.z, 0x7632);
@@ -266,7 +291,7 @@ TARFA_DEVI GemvTile gemv_tile(const GemvArgs& a, int tile, int nt_s, int tiles_r
 }
 
 template <typename T, int MODE, int PHASE, int KSPLIT, int NTB>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, gemv_ctas_per_sm(MODE, PHASE, NTB)) gemv_kernel(const GemvArgs a) {
   constexpr bool INT4 = MODE != kModeExact;
   constexpr int kGroups = kGemvWarps / KSPLIT;              // tiles per CTA step
   constexpr int TR = PHASE == kGateUp ? 8 : 16;             // tile rows per unit index
@@ -296,9 +321,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   // the shared unit's rows are fixed when the routing is the router's own top-k
   const UnitDesc fixed_sh{a.E, a.sh_row0, a.sh_rows, 0};
   const int tiles_r = a.N_r / TR, tiles_s = a.N_s / TR;
-  // shared-expert tiles first: they need no routing, so with in-kernel routing
-  // they run while the router kernel is still finishing
-  const int nt_s = (!INT4 && (a.which & 2) && has_sh) ? tiles_s : 0;
+  // shared-expert tiles first: they need no routing, so they run while the
+  // router kernel is still finishing.  The shared expert is never quantised:
+  // an int4 kernel runs its tiles with the exact loop and epilogue.
+  const int nt_s = ((a.which & 2) && has_sh) ? tiles_s : 0;
 
   for (int base = blockIdx.x * kGroups;; base += gridDim.x * kGroups) {
     if (nu < 0 && base + kGroups > nt_s) {   // CTA-uniform: first step with a routed tile
@@ -328,22 +354,25 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[b][q] = 0.f;
 
-      // token vector rows for this lane (B fragment column g of each token block)
+      // token vector rows for this lane (B fragment column g of each token
+      // block).  Columns past the unit's rows repeat its last row: their MMA
+      // outputs are never stored, and the loads need no guard.
       const char* xrow[NTB];
 #pragma unroll
       for (int b = 0; b < NTB; ++b) {
-        const int n = tg * 8 * NTB + b * 8 + g;
-        xrow[b] = nullptr;
-        if (n < ntok) {
-          const int r = d.row0 + n;
-          // shared-unit rows hold the tokens in order (perm_tok[row0 + n] == n)
-          const int xr = PHASE == kGateUp ? (shared_unit ? n : perm_tok[r]) : r;
-          const void* xb = shared_unit && a.x_sh ? a.x_sh : a.x;
-          xrow[b] = reinterpret_cast<const char*>(static_cast<const T*>(xb) + (int64_t)xr * a.ld_x);
-        }
+        const int n = min(tg * 8 * NTB + b * 8 + g, ntok - 1);
+        const int r = d.row0 + n;
+        // shared-unit rows hold the tokens in order (perm_tok[row0 + n] == n)
+        const int xr = PHASE == kGateUp ? (shared_unit ? n : perm_tok[r]) : r;
+        const void* xb = shared_unit && a.x_sh ? a.x_sh : a.x;
+        xrow[b] = reinterpret_cast<const char*>(static_cast<const T*>(xb) + (int64_t)xr * a.ld_x);
       }
 
-      {
+      if (INT4 && shared_unit) {
+        const int n_it = K / 32;
+        const int i0 = kw * n_it / KSPLIT, i1 = (kw + 1) * n_it / KSPLIT;
+        gemv_kloop<T, kModeExact, NTB>(rowA, rowB, scA, scB, a.group, i0, i1, xrow, acc);
+      } else {
         const int n_it = K / (INT4 ? 128 : 32);
         const int i0 = kw * n_it / KSPLIT, i1 = (kw + 1) * n_it / KSPLIT;
         gemv_kloop<T, MODE, NTB>(rowA, rowB, scA, scB, a.group, i0, i1, xrow, acc);
@@ -372,8 +401,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
 
       // -------- epilogue --------------------------------------------------------
       if (kw == 0) {
+        const bool fused4 = MODE == kModeInt4Fused && !shared_unit;
         float rsa = 1.f, rsb = 1.f;   // per-row int4 scale, folded after the dot
-        if (MODE == kModeInt4Fused && a.group == 0) {
+        if (fused4 && a.group == 0) {
           rsa = Elem<T>::bits_to_f(reinterpret_cast<const uint16_t*>(scA)[0]);
           rsb = Elem<T>::bits_to_f(reinterpret_cast<const uint16_t*>(scB)[0]);
         }
@@ -388,7 +418,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
             const float vb = acc[b][2 + q] * rsb;   // row g+8 (up   / down row g+8)
             if (PHASE == kGateUp) {
               float act;
-              if (MODE == kModeInt4Fused) {
+              if (fused4) {
                 // moe_kernel.py:99-100: silu(g) * u in fp32, one rounding
                 act = silu_f(va) * vb;
               } else {
@@ -400,7 +430,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
               *o = Elem<T>::from_f(act);
             } else {
               float* o = static_cast<float*>(a.out) + (int64_t)r * a.ld_out + tt * 16 + g;
-              if (MODE == kModeInt4Fused || a.raw_out) {
+              if (fused4 || a.raw_out) {
                 o[0] = va;            // moe_kernel.py:101-102: fp32 per-expert output
                 o[8] = vb;
               } else {

@@ -33,6 +33,7 @@ experts; every rank brings the same number of tokens per step.
 from __future__ import annotations
 
 import ctypes as C
+import copy
 import dataclasses
 
 import torch
@@ -291,9 +292,32 @@ class PeerExpertParallelMoE:
 
     __call__ = forward
 
+    def bind(self, shard: EPShard) -> "PeerExpertParallelMoE":
+        """This group (boxes, workspace, step counter) with another layer's
+        weights of the same shapes: the layers of a stack share one group and
+        run in order on one stream.  Not collective; every rank binds the same
+        layers and calls them in the same order.  The bound layer is released
+        with this one (its own ``close`` does nothing)."""
+        H, E, I, Is, K = self.dims
+        if shard.num_experts != E or shard.top_k != K or tuple(shard.router.shape) != (E, H):
+            raise ValueError("bound layer's router does not match the group's layer")
+        ops._need_cuda(shard.router, shard.bias)
+        E_loc, I_loc = ops._check_weights(shard.experts, H, self.dtype)
+        if E_loc != E // (self.world // self.tp) or I_loc * self.tp != I:
+            raise ValueError("bound layer's experts do not match the group's layer")
+        Is_b = shard.shared.gate_proj.shape[0] if shard.shared is not None else 0
+        if Is_b != Is:
+            raise ValueError("bound layer's shared expert does not match the group's layer")
+        b = copy.copy(self)
+        b.s = shard
+        b._wc = shard.experts.c_struct()
+        b._sc = shard.shared.c_struct() if shard.shared is not None else None
+        b._bound = True
+        return b
+
     def close(self):
         """Collective: unmap the peers' boxes, then free this rank's own."""
-        if self._box is None:
+        if getattr(self, "_bound", False) or self._box is None:
             return
         torch.cuda.synchronize(self.device)
         dist.barrier(self.group)

@@ -112,3 +112,76 @@ class SyntheticStack:
             routed = ops.experts_forward(x, idx, w, weights)
             h = h + (routed + ops.shared_expert(x, layer["shared"]))
         return lm_head_argmax(rms_norm(h, self.final_norm), self.lm_head)
+
+
+class ExpertParallelStack:
+    """The synthetic stack run expert-parallel over the ranks of ``group`` (one
+    process per GPU): the same model as :class:`SyntheticStack` built from the
+    same seed.  The embedding, norms, routers, shared experts and LM head are
+    replicated; rank ``r`` of ``N`` keeps experts ``[r*E/N, (r+1)*E/N)`` of
+    every layer resident.  Each MoE block is one call of the peer-memory
+    expert-parallel layer (``tarfa_b200_ep_moe_layer``); all layers share one
+    peer group (its boxes, workspace and step counter).
+
+    Construction and :meth:`close` are collective.  Every rank steps with its
+    own tokens, the same count on every rank, at most ``max_tokens``."""
+
+    def __init__(self, shape: syn.LayerShape, n_layers: int, vocab: int, device, seed: int = 0,
+                 group=None, max_tokens: int = 64, dtype=torch.bfloat16):
+        import torch.distributed as dist
+        from .ep import EPShard, PeerExpertParallelMoE
+        self.s, self.n, self.V = shape, n_layers, vocab
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.seed = seed
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        E = shape.experts
+        if E % world:
+            raise ValueError(f"{E} experts do not shard evenly over {world} ranks")
+        e0, e1 = rank * E // world, (rank + 1) * E // world
+        g = torch.Generator(device=self.device).manual_seed(syn._mix(seed, 0xE5))
+
+        def n(shape_, std):   # same draws, in the same order, as SyntheticStack
+            t = torch.empty(shape_, dtype=torch.float32, device=self.device)
+            t.normal_(0.0, std, generator=g)
+            return t.to(dtype)
+
+        self.embed = n((vocab, shape.hidden), 1.0)
+        self.lm_head = n((vocab, shape.hidden), 0.02)
+        self.final_norm = n((shape.hidden,), 0.1)
+        self.layers = []
+        for l in range(n_layers):
+            L = syn.layer_device(syn._mix(seed, l), shape, self.device, dtype)
+            mine = ops.ExpertWeights(L["gate_up"][e0:e1].clone(), L["down"][e0:e1].clone())
+            shared = ops.SharedWeights(L["sh_gate"], L["sh_up"], L["sh_down"], L["sh_gate_w"])
+            shard = EPShard(L["router"], mine, shared, E, shape.top_k)
+            del L
+            self.layers.append({"norm": n((shape.hidden,), 0.1), "shard": shard})
+        self._group = PeerExpertParallelMoE(self.layers[0]["shard"], group, max_tokens)
+        self.moe = [self._group] + [self._group.bind(x["shard"]) for x in self.layers[1:]]
+
+    def full_layer(self, l: int):
+        """All experts of layer ``l`` (regenerated from the seed) as single-GPU
+        weights, with its router and shared expert: (router, experts, shared)."""
+        L = syn.layer_device(syn._mix(self.seed, l), self.s, self.device, self.dtype)
+        sh = self.layers[l]["shard"]
+        return sh.router, ops.ExpertWeights(L["gate_up"], L["down"]), sh.shared
+
+    @torch.no_grad()
+    def step(self, tokens: torch.Tensor, record: list | None = None) -> torch.Tensor:
+        """One decode step of this rank's tokens -> next token ids (greedy).
+        ``record``: if given, gets each layer's (MoE input, MoE output)."""
+        h = self.embed.index_select(0, tokens.to(self.device))
+        for l, layer in enumerate(self.layers):
+            x = rms_norm(h, layer["norm"])
+            y = self.moe[l](x)
+            if record is not None:
+                record.append((x, y))
+            h = h + y
+        return lm_head_argmax(rms_norm(h, self.final_norm), self.lm_head)
+
+    def close(self):
+        """Collective: releases the peer group."""
+        if self._group is not None:
+            self._group.close()
+            self._group = None

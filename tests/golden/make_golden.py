@@ -1,6 +1,7 @@
 """Generate golden vectors by running the REFERENCE on the CPU (this container only).
 
-Run:  python tests/golden/make_golden.py [--ref /path/to/tarfa-checkout]
+Run:  python tests/golden/make_golden.py --ref /path/to/tarfa-checkout
+      (or set TARFA_REF to that path; one of the two is required)
 
 It imports the reference's own routed-experts closure
 (``tarfa/engine/fused_int4.py:148-262``, ``TarfaFused._install_streamed_experts``)
@@ -198,8 +199,13 @@ SMALL_ODD = syn.LayerShape(hidden=512, experts=40, inter=192, shared_inter=64)
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("TARFA_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("TARFA_REF"),
+                    help="root of a tarfa checkout (default: $TARFA_REF)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give the reference checkout with --ref or TARFA_REF")
+    if not os.path.isdir(os.path.join(a.ref, "tarfa", "engine")):
+        ap.error(f"{a.ref} has no tarfa/engine: not a tarfa checkout")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     fi, cq, mk = _load_reference(a.ref)
     cases = []

@@ -176,6 +176,50 @@ def test_ep_missing_peer_times_out():
             api.check(api.lib().tarfa_b200_ep_box_free(b))
 
 
+def _check_ep_stack(dev, rank):
+    """A small expert-parallel stack (collective): every layer's output equals
+    the single-GPU layer's on the same input, and so do the greedy tokens."""
+    from tarfa_b200 import ops, synthetic as syn
+    from tarfa_b200.stack import ExpertParallelStack, lm_head_argmax, rms_norm
+    ss = syn.LayerShape(hidden=256, experts=16, inter=128, shared_inter=128)
+    st = ExpertParallelStack(ss, 3, 512, dev, seed=9, max_tokens=8)
+    try:
+        for T in (1, 5):
+            tok = (torch.arange(T, device=dev) * 31 + 7 * rank) % 512
+            rec = []
+            nxt = st.step(tok, record=rec)
+            h = st.embed.index_select(0, tok)
+            for l in range(3):
+                w_r, full_l, sh = st.full_layer(l)
+                x = rms_norm(h, st.layers[l]["norm"])
+                assert torch.equal(x, rec[l][0]), f"rank {rank} T={T} layer {l}: input differs"
+                y = ops.moe_layer(x, w_r, full_l, sh)
+                assert torch.equal(y, rec[l][1]), f"rank {rank} T={T} layer {l}: output differs"
+                h = h + y
+            ref = lm_head_argmax(rms_norm(h, st.final_norm), st.lm_head)
+            assert torch.equal(ref, nxt), f"rank {rank} T={T}: greedy tokens differ"
+        assert ops.device_status() == 0
+    finally:
+        torch.cuda.synchronize()
+        st.close()
+
+
+def test_ep_stack_one_rank_equals_layers():
+    """The expert-parallel stack in a one-rank group (gloo for the handle
+    exchange): layer for layer the single-GPU layer."""
+    import torch.distributed as dist
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised in this process")
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{_free_port()}", rank=0,
+                            world_size=1)
+    try:
+        _check_ep_stack(dev, 0)
+    finally:
+        dist.destroy_process_group()
+
+
 def _free_port():
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
@@ -221,6 +265,7 @@ def _worker(rank, world, port, errq):
             del g
             assert ops.device_status() == 0
             ep.close()
+        _check_ep_stack(dev, rank)
         dist.barrier()
         dist.destroy_process_group()
     except Exception:

@@ -133,8 +133,9 @@ def _layer(E, H=256, I=64, Is=64, seed=0):
 
 @pytest.mark.parametrize("E,T", [(256, 1), (256, 4), (256, 16), (64, 16), (1024, 8), (256, 40)])
 def test_moe_layer_tie_order(E, T):
-    """Decode batches route inside the gate_up GEMV (T <= 16); 40 tokens take the
-    router kernel.  The layer output follows the same routing as the oracle."""
+    """Decode batches (T <= 16) route in the router's last CTA, interior tie
+    orders settled in the combine; 40 tokens take the router kernel.  The layer
+    output follows the same routing as the oracle."""
     rows = level_rows(T, E, 6, seed=E + T)
     if E in (256, 64):
         rows[: min(T, 4)] = adversarial_rows(E, 8, min(T, 4))
@@ -154,3 +155,39 @@ def test_moe_layer_tie_order(E, T):
     ref = mo.experts_exact(h, idx_o, w_o, lambda e: (gu[e], dn[e]), E) + mo.shared_expert(h, *sh)
     from gpu_helpers import assert_close
     assert_close(out, ref, f"layer on tied routing E={E} T={T}")
+
+
+@pytest.mark.parametrize("T", [1, 4])
+def test_expert_parallel_exchange_tie_order(T):
+    """The expert-parallel layer tops-k each token in its exchange kernel: a
+    one-rank group (gloo for the handle exchange) returns the oracle's ids in
+    order and the single-GPU layer's output."""
+    import socket
+    import torch.distributed as dist
+    from tarfa_b200.ep import EPShard, PeerExpertParallelMoE
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised in this process")
+    E = 256
+    rows = level_rows(T, E, 6, seed=50 + T)
+    rows[: min(T, 2)] = adversarial_rows(E, 8, min(T, 2))
+    h, w_r = planted(rows, H=256)
+    gu, dn, sh = _layer(E)
+    wts = ops.ExpertWeights(gu.to(DEV), dn.to(DEV))
+    shd = ops.SharedWeights(*[t.to(DEV) for t in sh])
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        ep = PeerExpertParallelMoE(EPShard(w_r.to(DEV), wts, shd, E), max_tokens=8)
+        try:
+            out, idx, _ = ep.forward(h.to(DEV), return_routing=True)
+            ref = ops.moe_layer(h.to(DEV), w_r.to(DEV), wts, shd)
+            torch.cuda.synchronize()
+            assert ops.device_status() == 0
+            assert torch.equal(idx.cpu(), expected(rows, 8))
+            assert torch.equal(out, ref)
+        finally:
+            ep.close()
+    finally:
+        dist.destroy_process_group()
