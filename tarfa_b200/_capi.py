@@ -74,6 +74,7 @@ SIGNATURES = {
     "tarfa_b200_combine_routes": (C.c_int, [C.POINTER(MoeShape), _P, _P, _P, _P, _P, _P]),
     "tarfa_b200_set_decode_routing_max_tokens": (C.c_int, [C.c_int64]),
     "tarfa_b200_stage_copy": (C.c_int, [_P, _P, C.c_size_t, _P]),
+    "tarfa_b200_rms_norm": (C.c_int, [_P, _P, C.c_int64, C.c_int64, C.c_double, C.c_int32, _P, _P]),
     "tarfa_b200_ep_box_bytes": (C.c_size_t, [C.POINTER(MoeShape), C.c_int32, C.c_int64]),
     "tarfa_b200_ep_workspace_size": (C.c_size_t, [C.POINTER(MoeShape), C.c_int32, C.c_int64]),
     "tarfa_b200_ep_box_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), _P]),

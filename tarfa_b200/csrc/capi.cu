@@ -19,6 +19,7 @@
 #include "int4.cuh"
 #include "router.cuh"
 #include "ep_p2p.cuh"
+#include "norm.cuh"
 
 using namespace tarfa;
 
@@ -1026,6 +1027,28 @@ int tarfa_b200_stage_copy(void* dst, const void* src, size_t bytes, void* stream
   stage_copy_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<uint4*>(const_cast<void*>(d)), static_cast<const uint4*>(sp), n16);
   TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
+}
+
+int tarfa_b200_rms_norm(const void* x, const void* w, int64_t rows, int64_t cols, double eps,
+                        int32_t dtype, void* out, void* stream) {
+  TARFA_CHECK(x && w && out, "null argument");
+  TARFA_CHECK(rows >= 0 && rows <= 0x7fffffff && cols > 0 && cols <= 16384,
+              "bad shape %lld x %lld (at most 16384 columns)", (long long)rows, (long long)cols);
+  if (rows == 0) return TARFA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t smem = (size_t)cols * sizeof(double);
+  if (dtype == TARFA_BF16)
+    TARFA_CUDA(launch_k(rms_norm_tree_kernel<__nv_bfloat16>, dim3((unsigned)rows), dim3(256), smem, st,
+                        false, static_cast<const __nv_bfloat16*>(x),
+                        static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out),
+                        (int)cols, eps));
+  else if (dtype == TARFA_F16)
+    TARFA_CUDA(launch_k(rms_norm_tree_kernel<__half>, dim3((unsigned)rows), dim3(256), smem, st, false,
+                        static_cast<const __half*>(x), static_cast<const __half*>(w),
+                        static_cast<__half*>(out), (int)cols, eps));
+  else
+    return fail(TARFA_ERR_INVALID, "dtype %d", dtype);
   return TARFA_OK;
 }
 

@@ -341,6 +341,22 @@ class MoePlan:
 _STAGE_COPY_MAX = 1 << 20
 
 
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """RMSNorm of the synthetic stack (``tarfa_b200_rms_norm``): fp64 with a
+    fixed pairwise tree for the sum of squares, rounded through fp32 to the
+    model dtype; bit-identical to :func:`tarfa_b200.stack.rms_norm_host`."""
+    _need_cuda(x, w)
+    if x.dtype not in _DT or w.dtype != x.dtype or w.numel() != x.shape[-1]:
+        raise RuntimeError("rms_norm: x [..., H] and w [H] in one model dtype")
+    x = x.contiguous()
+    w = w.contiguous()
+    out = torch.empty_like(x)
+    H = x.shape[-1]
+    api.check(api.lib().tarfa_b200_rms_norm(_ptr(x), _ptr(w), x.numel() // H, H, float(eps), _DT[x.dtype],
+                                            _ptr(out), _stream(x.device)))
+    return out
+
+
 def stage_copy(dst: torch.Tensor, src: torch.Tensor) -> None:
     """Kernel copy between device memory and pinned host memory (same shape and
     dtype, contiguous) on the current stream: for small transfers, faster than

@@ -39,14 +39,23 @@ def _tree_sum(v: torch.Tensor) -> torch.Tensor:
     return acc
 
 
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+def rms_norm_host(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """The stack's RMSNorm as torch operations (any device): the reference
+    statement of ``tarfa_b200_rms_norm``."""
     xd = x.double()
     r = 1.0 / torch.sqrt(_tree_sum(xd * xd) / x.shape[-1] + eps)
     return (xd * r * (1.0 + w.double())).to(torch.float32).to(x.dtype)
 
 
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """One kernel on the GPU (``ops.rms_norm``), torch operations on the CPU;
+    the same bits either way."""
+    return ops.rms_norm(x, w, eps) if x.is_cuda else rms_norm_host(x, w, eps)
+
+
 def lm_head_argmax(h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """Greedy token: argmax of the fp64 logits h @ w.T."""
+    """Greedy token: argmax of the fp64 logits h @ w.T (``w`` in the model dtype
+    or already in fp64)."""
     return (h.double() @ w.double().t()).argmax(-1)
 
 
@@ -157,6 +166,7 @@ class ExpertParallelStack:
             shard = EPShard(L["router"], mine, shared, E, shape.top_k)
             del L
             self.layers.append({"norm": n((shape.hidden,), 0.1), "shard": shard})
+        self._head64 = self.lm_head.double()   # converted once, not every step
         self._group = PeerExpertParallelMoE(self.layers[0]["shard"], group, max_tokens)
         self.moe = [self._group] + [self._group.bind(x["shard"]) for x in self.layers[1:]]
 
@@ -178,7 +188,7 @@ class ExpertParallelStack:
             if record is not None:
                 record.append((x, y))
             h = h + y
-        return lm_head_argmax(rms_norm(h, self.final_norm), self.lm_head)
+        return lm_head_argmax(rms_norm(h, self.final_norm), self._head64)
 
     def close(self):
         """Collective: releases the peer group."""
