@@ -543,9 +543,11 @@ int run_combine(const tarfa_moe_shape& s, const Ws& L, void* ws, const float* to
     c.idx_out = idx_out;
     smem = (size_t)tie_scratch_ints(c.E) * sizeof(int);
   }
-  // large batches: one block per token; decode: one-warp blocks, so that the
-  // few tokens' columns spread over many SMs (the loads are latency-bound)
-  const int threads = T_ > 64 ? kCombineTokenThreads : 32;
+  // large batches: one block per token, a thread per 8 columns (up to 512);
+  // decode: one-warp blocks, so that the few tokens' columns spread over many
+  // SMs (the loads are latency-bound)
+  const int threads =
+      T_ > 64 ? std::min(kCombineTokenThreads, ((H / 8 + 31) / 32) * 32) : 32;
   const dim3 grid(T_ > 64 ? 1 : (H / 8 + threads - 1) / threads, T_);
   if (gemm_y) TARFA_CUDA(launch_k(combine_token_kernel<T, T>, grid, dim3(threads), smem, st, pdl, c));
   else TARFA_CUDA(launch_k(combine_token_kernel<T, float>, grid, dim3(threads), smem, st, pdl, c));
