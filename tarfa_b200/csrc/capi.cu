@@ -146,7 +146,12 @@ struct Ws {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 constexpr size_t kZeroHeaderBytes = 2304;   // 16 + 16 + 8192/16*4, rounded to 256
-constexpr int64_t kRouterGemmMinTokens = 128;   // from here the router logits use the tensor cores
+// From here the router logits use the tensor cores (fp32 GEMM, then the exact
+// fix-up of logits near a rounding boundary).  Measured on the config-1 router:
+// 56 vs 160 us at 64 tokens, 54 vs 88 us at 32 (the exact CUDA-core router
+// scales with the tokens).  Smaller batches keep the CUDA-core router and its
+// smaller workspace.
+constexpr int64_t kRouterGemmMinTokens = 48;
 constexpr int kRouterMaxSplit = 8;             // K splits of the tensor-core router GEMM
 
 Ws layout(const tarfa_moe_shape& s, int op) {
@@ -588,41 +593,60 @@ int launch_permute(const Idx* idx, int T_, int K, int E, bool add_shared, const 
   return TARFA_OK;
 }
 
+bool use_router_gemm(const tarfa_moe_shape& s) {
+  return s.tokens >= kRouterGemmMinTokens && s.experts >= 128 && router_gemm_supported(s.hidden, s.experts);
+}
+
+// Exact logits of a batch on the tensor cores: fp32 partial logits (K split),
+// row norms of the router for the error window, then the window settles the
+// logits it can and lists the rest (and the shared-expert gate row), which are
+// recomputed exactly.  Leaves the list counter set: the next kernel that
+// reads the logits clears it (topk_kernel, or the expert-parallel exchange).
+template <typename T>
+int launch_router_logits_tc(const tarfa_moe_shape& s, const void* hidden, const void* w_r,
+                            const void* bias, const void* w_sg, const Ws& L, void* ws,
+                            float* logits_out, unsigned* status, int sms, cudaStream_t st) {
+  const int T_ = (int)s.tokens, H = (int)s.hidden, E = (int)s.experts;
+  const char* err = nullptr;
+  // split K so that the (tile, K range) work items fill the SMs about twice;
+  // shorter fp32 accumulations also narrow the fix-up window (fixup_rel)
+  const int64_t tiles = ((T_ + 127) / 128) * ((E + 255) / 256);
+  const int ksplit = (int)std::max<int64_t>(
+      1, std::min<int64_t>({(int64_t)kRouterMaxSplit, H / 64, 2 * sms / std::max<int64_t>(1, tiles)}));
+  if (router_logits_sm100(s.dtype == TARFA_BF16, hidden, T_, H, w_r, E, at<int32_t>(ws, L.units),
+                          at<float>(ws, L.lgpart), ksplit, status, sms, st, &err))
+    return fail(TARFA_ERR_CUDA, "%s", err ? err : "router logits");
+  row_norms_kernel<T><<<(E + 7) / 8, 256, 0, st>>>(static_cast<const T*>(w_r), E, H,
+                                                   at<float>(ws, L.wnorm));
+  const int grid = (T_ + 7) / 8;
+  unsigned* cnt = at<unsigned>(ws, L.fxcnt);
+  const T* hT = static_cast<const T*>(hidden);
+  const T* bT = static_cast<const T*>(bias);
+  fixup_window_kernel<T><<<grid, 256, 0, st>>>(
+      at<float>(ws, L.lgpart), ksplit, (int64_t)T_ * E, hT, bT, at<float>(ws, L.wnorm),
+      w_sg != nullptr, T_, H, E, at<float>(ws, L.logits), logits_out, at<int32_t>(ws, L.fxlist), cnt);
+  fixup_exact_kernel<T><<<sms * 8, 256, 0, st>>>(
+      hT, static_cast<const T*>(w_r), static_cast<const T*>(w_sg), bT, H, E,
+      at<int32_t>(ws, L.fxlist), cnt, at<float>(ws, L.logits), logits_out, at<float>(ws, L.gate_logit));
+  TARFA_CUDA(cudaGetLastError());
+  return TARFA_OK;
+}
+
 template <typename T>
 int launch_router(const tarfa_moe_shape& s, const void* hidden, const void* w_r, const void* bias,
                   const void* w_sg, const Ws& L, void* ws, int64_t* idx_out, float* w_out,
                   float* logits_out, bool permute, bool add_shared, unsigned* status,
                   cudaStream_t st) {
-  if (s.tokens >= kRouterGemmMinTokens && s.experts >= 128 &&
-      router_gemm_supported(s.hidden, s.experts)) {
-    // large batch: fp32 logits on the tensor cores, exact-rounding fixup + top-k, permute
+  if (use_router_gemm(s)) {
+    // batch: fp32 logits on the tensor cores, exact-rounding fixup + top-k, permute
     unsigned* st_ptr;
     int sms;
     if (int rc = device_info(&st_ptr, &sms)) return rc;
-    const int T_ = (int)s.tokens, H = (int)s.hidden, E = (int)s.experts, K = s.top_k;
-    const char* err = nullptr;
-    // split K so that the (tile, K range) work items fill the SMs about twice;
-    // shorter fp32 accumulations also narrow the fix-up window (fixup_rel)
-    const int64_t tiles = ((T_ + 127) / 128) * ((E + 255) / 256);
-    const int ksplit = (int)std::max<int64_t>(
-        1, std::min<int64_t>({(int64_t)kRouterMaxSplit, H / 64, 2 * sms / std::max<int64_t>(1, tiles)}));
-    if (router_logits_sm100(s.dtype == TARFA_BF16, hidden, T_, H, w_r, E, at<int32_t>(ws, L.units),
-                            at<float>(ws, L.lgpart), ksplit, status, sms, st, &err))
-      return fail(TARFA_ERR_CUDA, "%s", err ? err : "router logits");
-    row_norms_kernel<T><<<(E + 7) / 8, 256, 0, st>>>(static_cast<const T*>(w_r), E, H,
-                                                     at<float>(ws, L.wnorm));
-    // settle the logits the window decides, recompute the rest exactly (one warp
-    // per listed logit, load-balanced), then top-k
+    const int T_ = (int)s.tokens, E = (int)s.experts, K = s.top_k;
+    if (int rc = launch_router_logits_tc<T>(s, hidden, w_r, bias, w_sg, L, ws, logits_out, status, sms, st))
+      return rc;
     const int grid = (T_ + 7) / 8;
     unsigned* cnt = at<unsigned>(ws, L.fxcnt);
-    const T* hT = static_cast<const T*>(hidden);
-    const T* bT = static_cast<const T*>(bias);
-    fixup_window_kernel<T><<<grid, 256, 0, st>>>(
-        at<float>(ws, L.lgpart), ksplit, (int64_t)T_ * E, hT, bT, at<float>(ws, L.wnorm),
-        w_sg != nullptr, T_, H, E, at<float>(ws, L.logits), logits_out, at<int32_t>(ws, L.fxlist), cnt);
-    fixup_exact_kernel<T><<<sms * 8, 256, 0, st>>>(
-        hT, static_cast<const T*>(w_r), static_cast<const T*>(w_sg), bT, H, E,
-        at<int32_t>(ws, L.fxlist), cnt, at<float>(ws, L.logits), logits_out, at<float>(ws, L.gate_logit));
     TARFA_CUDA(launch_k(topk_kernel<T>, dim3(grid), dim3(256),
                         (size_t)8 * tie_scratch_ints(E) * sizeof(int), st, false,
                         at<float>(ws, L.logits), T_, E, K, at<int32_t>(ws, L.idx32),
@@ -790,8 +814,14 @@ EpWs ep_layout(const tarfa_moe_shape& s, int N, int64_t Tmax) {
   EpWs L{};
   size_t o = kZeroHeaderBytes;
   auto take = [&](size_t b) { size_t at = o; o += align256(b); return at; };
+  L.w.fxcnt = 2096;   // header: the router fix-up list length (tensor-core logits)
   L.w.logits = take(Tmax * E * 4);
   L.w.gate_logit = take(Tmax * 4);
+  if (Tmax >= kRouterGemmMinTokens) {   // tensor-core router logits for batches
+    L.w.wnorm = take(E * 4);
+    L.w.lgpart = take((size_t)kRouterMaxSplit * Tmax * E * 4);
+    L.w.fxlist = take((size_t)Tmax * (E + 1) * 4);
+  }
   L.w.idx32 = take(Tmax * K * 4);
   L.w.topw = take(Tmax * K * 4);
   L.w.units = take((4 + 4 * Umax) * 4);
@@ -843,11 +873,19 @@ int run_ep_layer(const tarfa_moe_shape& s, const void* hidden, const void* w_r, 
   const int rows_unit = N * T_;   // most rows of one unit (token batches of the GEMV)
 
   stage_mark(0, st);
-  if (int rc = launch_router_logits<T>(s, hidden, w_r, bias, sh ? sh->gate_weight : nullptr, L.w, ws,
-                                       sms, st))
+  // exact logits: the tensor-core router for batches, else the CUDA-core one
+  const bool tc_router = use_router_gemm(s) && grp.max_tokens >= kRouterGemmMinTokens;
+  if (tc_router) {
+    if (int rc = launch_router_logits_tc<T>(s, hidden, w_r, bias, sh ? sh->gate_weight : nullptr, L.w,
+                                            ws, nullptr, status, sms, st))
+      return rc;
+  } else if (int rc = launch_router_logits<T>(s, hidden, w_r, bias, sh ? sh->gate_weight : nullptr, L.w,
+                                              ws, sms, st)) {
     return rc;
+  }
   stage_mark(1, st);
   ep::Args a{};
+  a.fx_cnt = tc_router ? at<unsigned>(ws, L.w.fxcnt) : nullptr;
   a.T = T_;
   a.K = K;
   a.H = H;

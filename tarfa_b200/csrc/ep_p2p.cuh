@@ -91,6 +91,7 @@ struct Args {
   const float* gate_logit;     // [T] shared-expert gate logits (has_shared)
   void* out;                   // [T, H]
   unsigned* status;
+  unsigned* fx_cnt;            // tensor-core router's fix-up list length: cleared here, or null
 };
 
 TARFA_DEVI uint8_t* box_at(const Args& a, int r) { return static_cast<uint8_t*>(a.boxes[r]); }
@@ -201,6 +202,8 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_kernel(const Args a
   __shared__ int32_t s_idx[32];
   __shared__ float s_w[32];
   grid_dep_wait();                       // the router kernel's logits
+  // the tensor-core router's fix-up has read its list: leave its counter at zero
+  if (a.fx_cnt && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *a.fx_cnt = 0u;
   const Box B = box_layout(a.N, a.S, a.H);
   const unsigned step = read_step(a, B);
   const unsigned tag = step + 1;

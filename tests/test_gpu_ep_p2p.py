@@ -176,6 +176,44 @@ def test_ep_missing_peer_times_out():
             api.check(api.lib().tarfa_b200_ep_box_free(b))
 
 
+@pytest.mark.parametrize("T", [50, 64])
+def test_ep_one_rank_tensor_core_router(T):
+    """From 48 tokens (128 or more experts) the expert-parallel layer takes its
+    logits from the tensor-core router and its exact fix-up; the exchange then
+    tops-k them and clears the fix-up counter.  Two calls in a row equal the
+    single-GPU layer on the expert GEMVs (routing, weights and output)."""
+    from tarfa_b200 import _capi as api
+    from tarfa_b200 import ops
+    from tarfa_b200 import synthetic as syn
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    s = syn.LayerShape(hidden=1024, experts=128, inter=256, shared_inter=256)
+    L = syn.layer_device(5, s, dev)
+    full = ops.ExpertWeights(L["gate_up"], L["down"])
+    shared = ops.SharedWeights(L["sh_gate"], L["sh_up"], L["sh_down"], L["sh_gate_w"])
+    box = _alloc_box(s, 1, 64)
+    ops.set_gemm_min_tokens(1 << 30)   # the EP layer's experts run on the GEMV kernels
+    try:
+        ep = _CGroup(s, full, shared, L["router"], [box.value], 0, 64, 1)
+        gen = torch.Generator(device=dev).manual_seed(T)
+        for rep in range(2):
+            h = torch.randn((T, s.hidden), generator=gen, device=dev).to(torch.bfloat16)
+            out = torch.empty_like(h)
+            idx = torch.empty((T, 8), dtype=torch.int64, device=dev)
+            wt = torch.empty((T, 8), dtype=torch.float32, device=dev)
+            ep(h, out, idx, wt)
+            ref, ridx, rw = ops.moe_layer(h, L["router"], full, shared, return_routing=True)
+            torch.cuda.synchronize()
+            assert ops.device_status() == 0
+            assert torch.equal(idx, ridx), f"T={T} call {rep}: routing differs"
+            assert torch.equal(wt, rw), f"T={T} call {rep}: routing weights differ"
+            assert torch.equal(out, ref), f"T={T} call {rep}: output differs"
+    finally:
+        ops.set_gemm_min_tokens(64)
+        torch.cuda.synchronize()
+        api.check(api.lib().tarfa_b200_ep_box_free(box))
+
+
 def _check_ep_stack(dev, rank):
     """A small expert-parallel stack (collective): every layer's output equals
     the single-GPU layer's on the same input, and so do the greedy tokens."""

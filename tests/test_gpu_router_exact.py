@@ -70,9 +70,11 @@ def test_decode_router_exact_on_crafted_rows(dtype, T):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_prefill_router_exact_on_crafted_rows(dtype):
-    # 256 tokens and 128 experts take the tensor-core logits + fix-up route
-    h, w = crafted(256, 128, 512, dtype, seed=9)
+@pytest.mark.parametrize("T", [256, 64])
+def test_prefill_router_exact_on_crafted_rows(dtype, T):
+    # 48 tokens or more with 128 experts take the tensor-core logits + fix-up
+    # route (64: half of one 128-row tile)
+    h, w = crafted(T, 128, 512, dtype, seed=9)
     _check(h, w, 8)
 
 

@@ -113,9 +113,10 @@ def test_router_kernel_wide_spread(E):
     assert torch.equal(_router(rows, 8), expected(rows, 8))
 
 
-@pytest.mark.parametrize("E,levels", [(256, 4), (256, 40), (128, 10), (1024, 50)])
-def test_tensor_core_router_tie_order(E, levels):
-    rows = level_rows(256, E, levels, seed=E + levels)       # T >= 128: tcgen05 logits + top-k kernel
+@pytest.mark.parametrize("E,levels,T", [(256, 4, 256), (256, 40, 256), (128, 10, 256), (1024, 50, 256),
+                                          (256, 12, 64)])
+def test_tensor_core_router_tie_order(E, levels, T):
+    rows = level_rows(T, E, levels, seed=E + levels)         # T >= 48: tcgen05 logits + top-k kernel
     if E == 256:
         rows[:16] = adversarial_rows(E, 8, 16)
         rows[16:32] = wide_rows(16, E, seed=3)
