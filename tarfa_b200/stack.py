@@ -112,14 +112,16 @@ class SyntheticStack:
         h = self.embed.index_select(0, tokens.to(self.device))
         for l, layer in enumerate(self.layers):
             x = rms_norm(h, layer["norm"])
-            idx, w = ops.router_topk(x, layer["router"], self.s.top_k)
-            ids = torch.unique(idx).tolist()       # routed ids on the host (fused_int4.py:166)
+            idx, _ = ops.router_topk(x, layer["router"], self.s.top_k)
+            ids = sorted(set(idx.view(-1).tolist()))   # routed ids on the host (fused_int4.py:166)
             weights = self.tier.weights_for(l, ids)
             if prefetch and l + 1 < self.n and self._prev[l + 1] is not None:
                 self.tier.prefetch(l + 1, self._prev[l + 1])   # PIPE-style prediction
             self._prev[l] = ids
-            routed = ops.experts_forward(x, idx, w, weights)
-            h = h + (routed + ops.shared_expert(x, layer["shared"]))
+            # the whole block over the staged experts (the router again: exact, so
+            # the same routes); the same arithmetic as the expert-parallel stack's
+            # layers, which equal this layer bit for bit
+            h = h + ops.moe_layer(x, layer["router"], weights, layer["shared"], self.s.top_k)
         return lm_head_argmax(rms_norm(h, self.final_norm), self.lm_head)
 
 
