@@ -107,15 +107,33 @@ class SyntheticStack:
         return gu, dn
 
     @torch.no_grad()
-    def step(self, tokens: torch.Tensor, prefetch: bool = True) -> torch.Tensor:
-        """One decode step for a batch of token ids -> next token ids (greedy)."""
+    def step(self, tokens: torch.Tensor, prefetch="pipe") -> torch.Tensor:
+        """One decode step for a batch of token ids -> next token ids (greedy).
+
+        ``prefetch``: which of the next layer's experts to start copying while
+        this layer computes.  "pipe": the ones the next layer used for the
+        previous step (the reference's PIPE prediction, fused_int4.py:206-224).
+        "pregate": the next layer's router applied to this layer's input (its
+        ids come back with this layer's, in one host read); the residual stream
+        changes little per layer, so it mostly names the next layer's experts.
+        None: no prefetch.  The prediction only moves copies earlier: each
+        layer still routes exactly and stages whatever it misses."""
         h = self.embed.index_select(0, tokens.to(self.device))
         for l, layer in enumerate(self.layers):
             x = rms_norm(h, layer["norm"])
             idx, _ = ops.router_topk(x, layer["router"], self.s.top_k)
-            ids = sorted(set(idx.view(-1).tolist()))   # routed ids on the host (fused_int4.py:166)
+            pregate = prefetch == "pregate" and l + 1 < self.n
+            if pregate:
+                nidx, _ = ops.router_topk(x, self.layers[l + 1]["router"], self.s.top_k)
+                both = torch.cat([idx.view(-1), nidx.view(-1)]).tolist()   # one host read
+                k = idx.numel()
+                ids, pred = sorted(set(both[:k])), sorted(set(both[k:]))
+            else:
+                ids = sorted(set(idx.view(-1).tolist()))   # routed ids on the host (fused_int4.py:166)
             weights = self.tier.weights_for(l, ids)
-            if prefetch and l + 1 < self.n and self._prev[l + 1] is not None:
+            if pregate:
+                self.tier.prefetch(l + 1, pred)
+            elif prefetch and l + 1 < self.n and self._prev[l + 1] is not None:
                 self.tier.prefetch(l + 1, self._prev[l + 1])   # PIPE-style prediction
             self._prev[l] = ids
             # the whole block over the staged experts (the router again: exact, so
